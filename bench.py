@@ -1,0 +1,435 @@
+"""Benchmark of the causal depthwise conv1d path (forward + backward) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+
+Workload (the sweep the headline metric is quoted on, at its largest
+sequence length): per GPU x bf16 (B=8, T=32768, D=1024) ~ N(0,1), weight fp32 (1024, 4) ~ N(0, 1/4),
+bias fp32 ~ N(0, 0.1), activation SiLU, dout bf16 ~ N(0,1); seed 0, generated on the host and copied
+to the device. One step = forward + backward (dx, dweight, dbias). With N GPUs each rank runs its own
+batch shard of 8 rows (weak scaling) and the fp32 dweight||dbias vector is all-reduced over NCCL
+every step. Every tensor (537 MB) is larger than the 126 MB L2, so no flush is needed between steps.
+
+`value` is the aggregate algorithmic HBM throughput (GB/s, bytes as below) over all GPUs with inputs
+resident in HBM, from CUDA events around exactly K steps, max over ranks. `e2e` is the same metric
+measured through the public API (`causal_conv1d_fn` + autograd) with the step's inputs copied from
+pinned host memory and its results (out, dx, dweight, dbias) copied back inside the timed region.
+
+Algorithmic bytes per call (bf16 x/out/dout/dx = 2 B, fp32 weight/bias):
+  forward  = B*T*D*(2 + 2) + D*W*4 + D*4
+  backward = B*T*D*(2 + 2 + 2) + 2*(D*W*4 + D*4)
+
+--impl reference times the reference algorithm on the host CPU: the oracle (oracle/, a C
+restatement of the reference's per-element algorithm; the reference itself is Python/Triton and has
+no CPU implementation), with all host threads, on a bounded sample of the workload per step.
+--impl triton times the reference's own Triton kernels (baseline/_ref) on the same B200.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "causal-conv1d-triton_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "fwd/bwd HBM GB/s (% of ~8 TB/s) and µs/call, bf16 D=1024 W=4"
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+# Per-launch DRAM traffic (read + write bytes) of the backward kernel from one ncu capture of the
+# small case (B=8, T=8192, D=1024), scaled by units to this workload; see profiles/. None until
+# measured.
+BWD_DRAM_BYTES_PER_LAUNCH = None
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "triton"])
+    ap.add_argument("--batch", type=int, default=8, help="batch rows per GPU")
+    ap.add_argument("--seqlen", type=int, default=32768)
+    ap.add_argument("--dim", type=int, default=1024)
+    ap.add_argument("--width", type=int, default=4)
+    ap.add_argument("--no-bias-silu", action="store_true", help="the no-bias/no-activation mode")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget")
+    return ap.parse_args()
+
+
+def algo_bytes(B, T, D, W, es=2):
+    fwd = B * T * D * (es + es) + D * W * 4 + D * 4
+    bwd = B * T * D * (3 * es) + 2 * (D * W * 4 + D * 4)
+    return fwd, bwd
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def make_inputs(B, T, D, W, bias_silu, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+    w = torch.randn(D, W, generator=g) * 0.5
+    b = torch.randn(D, generator=g) * (0.1**0.5) if bias_silu else None
+    dy = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+    return x, w, b, dy
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons every 100 ms in the background."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), line.strip()))
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return {"unavailable": "nvidia-smi not runnable"}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sel = [r for t, r in self.rows if self.t0 - 0.15 <= t <= self.t1 + 0.15] or [r for _, r in self.rows]
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in sel:
+            f = [c.strip() for c in r.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                sms.append(float(f[2]))
+                maxs.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[6:10]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sms:
+            return {"unavailable": "no samples"}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs), "samples": len(sms),
+                "reasons": sorted(reasons)}
+
+
+def cpu_sample_gbs(w, b, x, dy, silu, seconds, nthreads=0, rows=None):
+    """Times the oracle (fwd + bwd) on batch row 0 (optionally its first `rows` time rows) until
+    `seconds` have passed; returns (GB/s of algorithmic bytes, sample description, reps)."""
+    from oracle import oracle
+
+    xs = x[:1] if rows is None else x[:1, :rows]
+    dys = dy[:1] if rows is None else dy[:1, :rows]
+    xs32, dys32 = xs.float().numpy(), dys.float().numpy()
+    _, T, D = xs.shape
+    W = w.shape[1]
+    fb, bb = algo_bytes(1, T, D, W)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.fwd(xs32, w, b, None, None, silu=silu, nthreads=nthreads)
+        oracle.bwd(xs32, w, b, None, None, dys32, None, False, silu=silu, nthreads=nthreads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return (fb + bb) * reps / el / 1e9, f"batch row 0, T={T}, D={D}: fwd+bwd x{reps} in {el:.1f} s", reps
+
+
+def run_reference_cpu(args):
+    """--impl reference: the reference algorithm on the host cores (the oracle port)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    B, T, D, W = args.batch, args.seqlen, args.dim, args.width
+    bias_silu = not args.no_bias_silu
+    x, w, b, dy = make_inputs(B, T, D, W, bias_silu)
+    rows = min(T, 2048)  # bounded sample per step: batch row 0, first 2048 time rows
+    xs, dys = x[:1, :rows].float().numpy(), dy[:1, :rows].float().numpy()
+    cores = os.cpu_count()
+    fb, bb = algo_bytes(1, rows, D, W)
+
+    def step():
+        oracle.fwd(xs, w, b, None, None, silu=bias_silu)
+        oracle.bwd(xs, w, b, None, None, dys, None, False, silu=bias_silu)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    gbs = (fb + bb) * args.steps / el / 1e9
+    sample = f"per step: batch row 0, T[0:{rows}], D={D}, W={W}, fwd+bwd"
+    print(json.dumps({
+        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "impl": "reference",
+        "data": "synthetic, seed 0",
+        "config": workload_config(args),
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def workload_config(args):
+    n = args.gpus
+    return {
+        "workload": f"BASELINE config 2 (sweep), B={args.batch}/GPU T={args.seqlen} D={args.dim} "
+                    f"W={args.width} {'none' if args.no_bias_silu else 'bias+silu'}, fwd+bwd step",
+        "global_batch": args.batch * n, "seq_len": args.seqlen, "dim": args.dim,
+        "width": args.width,
+        "parallelism": f"dp{n}: batch shards, NCCL all-reduce of fp32 dweight||dbias" if n > 1 else "single GPU",
+        "l2": "no flush: every tensor is larger than L2 (126 MB)",
+    }
+
+
+def run_triton_reference(args, dev):
+    """--impl triton: the reference's Triton kernels (baseline/_ref) on this GPU."""
+    sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+    import causal_conv1d_triton.causal_conv1d as ref
+
+    return ref._fwd, ref._bwd
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference_cpu(args)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    B, T, D, W = args.batch, args.seqlen, args.dim, args.width
+    bias_silu = not args.no_bias_silu
+    x_h, w_h, b_h, dy_h = make_inputs(B, T, D, W, bias_silu, seed=rank)
+    x, w = x_h.to(dev), w_h.to(dev)
+    b = b_h.to(dev) if b_h is not None else None
+    dy = dy_h.to(dev)
+    fbytes, bbytes = algo_bytes(B, T, D, W)
+
+    if args.impl == "triton":
+        fwd_fn, bwd_fn = run_triton_reference(args, dev)
+
+        def fwd():
+            return fwd_fn(x, w, b, None, None, None, bias_silu)
+
+        def bwd():
+            return bwd_fn(x, w, b, None, None, dy, None, False, bias_silu)
+        grad_buf = None
+    else:
+        from causal_conv1d_b200.causal_conv1d import _bwd, _fwd
+
+        grad_buf = torch.zeros(D * (W + 1), device=dev, dtype=torch.float32) if world > 1 else None
+
+        def fwd():
+            return _fwd(x, w, b, None, None, None, bias_silu)
+
+        def bwd():
+            r = _bwd(x, w, b, None, None, dy, None, False, bias_silu, grad_f32=grad_buf)
+            if world > 1:
+                dist.all_reduce(grad_buf)
+            return r
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        fwd()
+        bwd()
+    torch.cuda.synchronize(dev)
+
+    n_ev = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_ev)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.mark_start()
+    start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        fwd()
+        ev[i][1].record(stream)
+        bwd()
+        ev[i][2].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    sampler.mark_end()
+    if dist is not None:
+        dist.barrier()
+    clocks = sampler.stop()
+    total_ms = start.elapsed_time(end)
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / n_ev
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / n_ev
+    if dist is not None:
+        t = torch.tensor([total_ms, fwd_ms, bwd_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, fwd_ms, bwd_ms = t.tolist()
+
+    ms_step = total_ms / args.steps
+    value = (fbytes + bbytes) * world / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    fwd_gbs = fbytes / (fwd_ms * 1e-3) / 1e9
+    bwd_gbs = bbytes / (bwd_ms * 1e-3) / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: x, dout ~ N(0,1) bf16; weight ~ N(0,1/4), bias ~ N(0,0.1) fp32; seed = rank",
+        "config": workload_config(args),
+        "fwd": {"us_per_call": fwd_ms * 1e3, "gbs": fwd_gbs, "frac_of_8tbs": fwd_gbs / NOMINAL_HBM_GBS,
+                "frac_of_measured": fwd_gbs / peak},
+        "bwd": {"us_per_call": bwd_ms * 1e3, "gbs": bwd_gbs, "frac_of_8tbs": bwd_gbs / NOMINAL_HBM_GBS,
+                "frac_of_measured": bwd_gbs / peak,
+                "note": "backward kernel + fixed-order partial reduce" + (" + NCCL all-reduce" if world > 1 else "")},
+        "clocks": clocks,
+    }
+    if args.impl == "triton":
+        line["impl"] = "reference-triton"
+        line["gpu_launches"] = 0
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    line["impl"] = "ours"
+    line["gpu_launches"] = 3 * args.steps
+    line["roofline"] = {
+        "bound": "hbm", "kernel": "cc1d_bwd_tma_kernel (+ reduce)", "achieved": bwd_gbs,
+        "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak, "peak_source": f"{peak_kind} hbm_gbs",
+        "traffic": BWD_DRAM_BYTES_PER_LAUNCH * (B * T) / (8 * 8192) if BWD_DRAM_BYTES_PER_LAUNCH else None,
+        "algorithmic_bytes": bbytes,
+    }
+
+    # End to end through the public API, host buffers in and out.
+    line["e2e"] = e2e(args, dev, x_h, w_h, b_h, dy_h, bias_silu, world, dist)
+
+    if rank == 0:
+        cores = torch.get_num_threads()
+        gbs, sample, _ = cpu_sample_gbs(w_h, b_h, x_h, dy_h, bias_silu, args.cpu_seconds, nthreads=0)
+        line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": os.cpu_count(),
+                                "kind": "port", "sample": sample,
+                                "torch_threads": cores}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def e2e(args, dev, x_h, w_h, b_h, dy_h, bias_silu, world, dist):
+    from causal_conv1d_b200 import causal_conv1d_fn
+
+    xp, dyp = x_h.pin_memory(), dy_h.pin_memory()
+    out_h = torch.empty_like(x_h).pin_memory()
+    dx_h = torch.empty_like(x_h).pin_memory()
+    dw_h = torch.empty_like(w_h).pin_memory()
+    db_h = torch.empty_like(b_h).pin_memory() if b_h is not None else None
+    w = w_h.to(dev).requires_grad_(True)
+    b = b_h.to(dev).requires_grad_(True) if b_h is not None else None
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        x = xp.to(dev, non_blocking=True).requires_grad_(True)
+        dy = dyp.to(dev, non_blocking=True)
+        w.grad = None
+        if b is not None:
+            b.grad = None
+        out = causal_conv1d_fn(x, w, b, activation="silu" if bias_silu else None)
+        out.backward(dy)
+        if world > 1:
+            g = torch.cat([w.grad.flatten()] + ([b.grad] if b is not None else []))
+            dist.all_reduce(g)
+        out_h.copy_(out, non_blocking=True)
+        dx_h.copy_(x.grad, non_blocking=True)
+        dw_h.copy_(w.grad, non_blocking=True)
+        if b is not None:
+            db_h.copy_(b.grad, non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(args.e2e_steps):
+        step()
+    e.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = s.elapsed_time(e) / args.e2e_steps
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    B, T, D = x_h.shape
+    W = w_h.shape[1]
+    fb, bb = algo_bytes(B, T, D, W)
+    h2d = xp.numel() * 2 + dyp.numel() * 2
+    d2h = out_h.numel() * 2 + dx_h.numel() * 2 + dw_h.numel() * 4 + (db_h.numel() * 4 if db_h is not None else 0)
+    return {"value": (fb + bb) * world / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms,
+            "steps": args.e2e_steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+
+if __name__ == "__main__":
+    main()

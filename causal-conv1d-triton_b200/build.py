@@ -1,0 +1,94 @@
+"""Builds libcausal_conv1d_b200.so (the C-ABI library of include/causal_conv1d_b200.h) for
+sm_100a with nvcc, in-tree: objects under _build/, the library inside the Python package.
+
+    python causal-conv1d-triton_b200/build.py [--force] [--verbose]
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "causal_conv1d_b200", "libcausal_conv1d_b200.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + [
+    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
+    "-I", INCLUDE, "-I", CSRC,
+]
+
+
+def _nvcc() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found; the CUDA toolkit is required to build")
+    return cand
+
+
+def sources():
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+
+
+def _headers():
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
+    return hs + [os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE) if f.endswith(".h")]
+
+
+def _stale(target, deps) -> bool:
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> str:
+    """Compiles every .cu under csrc/ for sm_100a and links the shared library; returns its path."""
+    os.makedirs(BUILD, exist_ok=True)
+    nvcc = _nvcc()
+    headers = _headers()
+    srcs = sources()
+    objs = [os.path.join(BUILD, os.path.basename(s)[:-3] + ".o") for s in srcs]
+    todo = [(s, o) for s, o in zip(srcs, objs) if force or ptxas_verbose or _stale(o, [s] + headers)]
+
+    def compile_one(so):
+        s, o = so
+        cmd = [nvcc] + NVCC_FLAGS + (["-Xptxas", "-v"] if ptxas_verbose else []) + ["-c", s, "-o", o]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {s}:\n{r.stdout}\n{r.stderr}")
+        return s, r.stderr
+
+    if todo:
+        with cf.ThreadPoolExecutor(max_workers=min(len(todo), os.cpu_count() or 4)) as ex:
+            for s, err in ex.map(compile_one, todo):
+                if ptxas_verbose and err:
+                    print(f"== {os.path.basename(s)}\n{err}", flush=True)
+    if force or todo or _stale(LIB, objs):
+        cmd = [nvcc] + ARCH + ["-shared", "-o", LIB] + objs
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--ptxas-verbose", action="store_true", help="print registers/spills per kernel")
+    a = ap.parse_args()
+    print(build(a.force, a.verbose, a.ptxas_verbose))
+    sys.exit(0)

@@ -1,0 +1,246 @@
+"""Causal depthwise conv1d over channels-last inputs, with forward and backward, on B200 (sm_100a).
+
+    out[b, t, d] = act(bias[d] + sum_k weight[d, k] * x[b, t - (W - 1) + k, d])
+
+where positions t < 0 read `initial_states` (or zero). A drop-in replacement for
+jxiong21029/causal-conv1d-triton's `causal_conv1d_fn` (causal_conv1d_triton/causal_conv1d.py:579-639):
+same signature, argument meaning, asserts and return values. x is (batch, seqlen, dim) and the
+states are (batch, width - 1, dim): the inputs preceding x[:, 0]. Any width >= 2 (up to 256);
+fp32/fp16/bf16 inputs, fp32 accumulation.
+
+The kernels are hand-written CUDA for sm_100a behind the C ABI of include/causal_conv1d_b200.h,
+called through ctypes (`_native`). This module keeps the host-side logic of the reference: the
+argument checks, the autograd Function, and the empty-input cases.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from . import _native
+from ._native import DTYPE_CODE, check, lib
+
+_FLOAT = (torch.float32, torch.float16, torch.bfloat16)
+
+
+def _check_inputs(x, weight, bias, seq_idx, initial_states):
+    """The reference's shape/device asserts (causal_conv1d.py:397-408)."""
+    assert x.ndim == 3, "x must be (batch, seqlen, dim)"
+    B, T, D = x.shape
+    assert weight.ndim == 2 and weight.shape[0] == D, "weight must be (dim, width)"
+    W = weight.shape[1]
+    assert W >= 2, "width must be >= 2"
+    assert x.is_cuda and weight.device == x.device
+    assert bias is None or bias.shape == (D,)
+    assert initial_states is None or initial_states.shape == (B, W - 1, D)
+    assert seq_idx is None or seq_idx.shape == (B, T)
+    # The reference computes offsets within one batch element in int32; the same inputs are
+    # rejected here so that both accept exactly the same calls.
+    assert (T + W) * max(x.stride(1), D) < 2**31
+
+
+def _channels_contiguous(t: Tensor) -> Tensor:
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _as_float(t: Tensor | None) -> Tensor | None:
+    """Parameters in a float type the kernels do not read (e.g. float64) are passed as fp32."""
+    if t is None or t.dtype in _FLOAT:
+        return t
+    return t.float()
+
+
+def _ptr(t: Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _code(t: Tensor | None) -> int:
+    return 0 if t is None else DTYPE_CODE[t.dtype]
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _DeviceGuard:
+    """Makes `device` current for the C calls, which launch on the current device (the reference
+    launches under torch.cuda.device(x.device), causal_conv1d.py:448)."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, device):
+        self.idx = device.index
+
+    def __enter__(self):
+        self.prev = torch.cuda.current_device()
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.prev)
+
+
+def _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu):
+    """Host launcher of the forward (the reference's `_fwd`, causal_conv1d.py:433-472)."""
+    if x.dtype not in _FLOAT:
+        raise TypeError(f"x must be float32, float16 or bfloat16, got {x.dtype}")
+    B, T, D = x.shape
+    W = weight.shape[1]
+    out = torch.empty(B, T, D, device=x.device, dtype=x.dtype)
+    w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
+    with _DeviceGuard(x.device):
+        check(
+            lib.cc1d_fwd(
+                x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
+                _ptr(seq_idx), out.data_ptr(), _ptr(final_states), B, T, D, W,
+                DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
+                _stream(x.device),
+            ),
+            "causal_conv1d forward",
+        )
+    return out
+
+
+def _bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_dinit, silu,
+         grad_f32=None):
+    """Host launcher of the backward (the reference's `_bwd`, causal_conv1d.py:475-541).
+
+    Returns (dx, dweight, dbias, dinit). With `grad_f32` (a contiguous fp32 tensor of D * (W + 1)
+    elements) the weight/bias gradients are written there as [dweight (D, W), dbias (D)] instead,
+    and dweight/dbias are returned as None.
+    """
+    B, T, D = x.shape
+    W = weight.shape[1]
+    dx = torch.empty(B, T, D, device=x.device, dtype=x.dtype)
+    dinit = torch.empty_like(initial_states) if need_dinit else None
+    w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
+    dinit_k = _as_float(dinit)
+    if grad_f32 is None:
+        dweight = torch.empty_like(w)
+        dbias = torch.empty_like(b) if b is not None else None
+    else:
+        dweight = dbias = None
+    if dfinal_states is not None and dfinal_states.dtype != x.dtype:
+        dfinal_states = dfinal_states.to(x.dtype)
+    with _DeviceGuard(x.device):
+        ws_bytes = lib.cc1d_bwd_workspace_bytes(
+            x.data_ptr(), x.stride(0), x.stride(1), dout.data_ptr(), dout.stride(0),
+            dout.stride(1), B, T, D, W, DTYPE_CODE[x.dtype],
+        )
+        if ws_bytes < 0:
+            check(_native.CC1D_ERR_INVALID, "causal_conv1d backward workspace")
+        workspace = torch.empty(max(1, ws_bytes // 4), device=x.device, dtype=torch.float32)
+        check(
+            lib.cc1d_bwd(
+                x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
+                _ptr(seq_idx), dout.data_ptr(), dout.stride(0), dout.stride(1),
+                _ptr(dfinal_states), dx.data_ptr(), _ptr(dweight), _ptr(dbias), _ptr(dinit_k),
+                _ptr(grad_f32), workspace.data_ptr(), ws_bytes, B, T, D, W,
+                DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
+                _stream(x.device),
+            ),
+            "causal_conv1d backward",
+        )
+    if dinit is not None and dinit_k is not dinit:
+        dinit.copy_(dinit_k)
+    if grad_f32 is None:
+        if dweight.dtype != weight.dtype:
+            dweight = dweight.to(weight.dtype)
+        if dbias is not None and dbias.dtype != bias.dtype:
+            dbias = dbias.to(bias.dtype)
+    return dx, dweight, dbias, dinit
+
+
+class _CausalConv1dFn(torch.autograd.Function):
+    """Autograd wrapper (the reference's `_CausalConv1dFn`, causal_conv1d.py:544-576)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, seq_idx, initial_states, return_final_states, silu):
+        final_states = None
+        if return_final_states:
+            final_states = torch.empty(
+                x.shape[0], weight.shape[1] - 1, x.shape[2], device=x.device, dtype=x.dtype
+            )
+        out = _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu)
+        ctx.save_for_backward(x, weight, bias, seq_idx, initial_states)
+        ctx.silu = silu
+        ctx.return_final_states = return_final_states
+        return (out, final_states) if return_final_states else out
+
+    @staticmethod
+    def backward(ctx, dout, *args):
+        x, weight, bias, seq_idx, initial_states = ctx.saved_tensors
+        dfinal_states = args[0] if ctx.return_final_states else None
+        if dfinal_states is not None:
+            dfinal_states = dfinal_states.contiguous()
+        need_dinit = initial_states is not None and ctx.needs_input_grad[4]
+        dx, dweight, dbias, dinit = _bwd(
+            x, weight, bias, seq_idx, initial_states, _channels_contiguous(dout), dfinal_states,
+            need_dinit, ctx.silu,
+        )
+        return dx, dweight, dbias, None, dinit, None, None
+
+
+def causal_conv1d_fn(
+    x: Tensor,
+    weight: Tensor,
+    bias: Tensor | None = None,
+    seq_idx: Tensor | None = None,
+    initial_states: Tensor | None = None,
+    return_final_states: bool = False,
+    final_states_out: Tensor | None = None,
+    activation: str | None = None,
+) -> Tensor | tuple[Tensor, Tensor]:
+    """Causal depthwise conv1d over channels-last inputs.
+
+    x: (batch, seqlen, dim); must be contiguous along dim
+    weight: (dim, width), width >= 2
+    bias: (dim,)
+    seq_idx: (batch, seqlen) integer sequence ids for packed sequences. Positions with negative ids
+        are considered padding, and give zero outputs. Can be combined with initial_states, which
+        count as part of seq_idx[:, 0]'s sequence, but cannot be combined with return_final_states
+    initial_states: (batch, width - 1, dim), the inputs preceding x[:, 0]
+    return_final_states: also return the last width - 1 rows of concat(initial_states, x), i.e. the
+        initial_states for continuing the sequence; supports grad
+    final_states_out: optional (batch, width - 1, dim) buffer to copy the final states into
+    activation: None, "silu", or "swish"
+
+    Returns out of shape (batch, seqlen, dim) and dtype x.dtype, or (out, final_states).
+    """
+    if activation not in (None, "silu", "swish"):
+        raise NotImplementedError("activation must be None, silu, or swish")
+    if seq_idx is not None:
+        assert not return_final_states, "cannot return final states if seq_idx is not None"
+    if final_states_out is not None:
+        assert return_final_states, "final_states_out requires return_final_states=True"
+    _check_inputs(x, weight, bias, seq_idx, initial_states)
+
+    x = _channels_contiguous(x)
+    weight = weight.contiguous()
+    bias = bias.contiguous() if bias is not None else None
+    seq_idx = seq_idx.to(torch.int32).contiguous() if seq_idx is not None else None
+    initial_states = initial_states.contiguous() if initial_states is not None else None
+    silu = activation is not None
+
+    needs_grad = torch.is_grad_enabled() and any(
+        t is not None and t.requires_grad for t in (x, weight, bias, initial_states)
+    )
+    if needs_grad:
+        result = _CausalConv1dFn.apply(
+            x, weight, bias, seq_idx, initial_states, return_final_states, silu
+        )
+    else:
+        final_states = None
+        if return_final_states:
+            final_states = torch.empty(
+                x.shape[0], weight.shape[1] - 1, x.shape[2], device=x.device, dtype=x.dtype
+            )
+        out = _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu)
+        result = (out, final_states) if return_final_states else out
+
+    if final_states_out is not None:
+        out, final_states = result
+        result = out, final_states_out.copy_(final_states)
+    return result

@@ -1,0 +1,438 @@
+// C ABI of the causal depthwise conv1d library: argument checks, path selection (TMA kernels for
+// widths 2..8 on 16-byte-aligned layouts, generic kernels otherwise), tensor-map encoding, grid
+// sizing from the measured occupancy and SM count, and the T == 0 cases. Declared in
+// include/causal_conv1d_b200.h, where each entry point names the reference launch it replaces.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "causal_conv1d_b200.h"
+#include "cc1d_dispatch.h"
+#include "cc1d_reduce_kernels.cuh"
+
+namespace cc1d {
+
+__device__ unsigned g_status_word;
+
+namespace {
+
+thread_local int t_last_cuda_error = 0;
+
+int cuda_fail(cudaError_t e) {
+  t_last_cuda_error = static_cast<int>(e);
+  return CC1D_ERR_CUDA;
+}
+
+#define CC1D_TRY_CUDA(call)                    \
+  do {                                         \
+    const cudaError_t e_ = (call);             \
+    if (e_ != cudaSuccess) return cuda_fail(e_); \
+  } while (0)
+
+#define CC1D_TRY(call)        \
+  do {                        \
+    const int r_ = (call);    \
+    if (r_ != CC1D_OK) return r_; \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sms = 0;
+  unsigned* status = nullptr;  // device address of g_status_word on this device
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+bool g_dev_ready[kMaxDevices] = {};
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::map<std::tuple<const void*, int, int>, int> g_occupancy;  // (fn, device, smem) -> CTAs/SM
+std::map<std::pair<const void*, int>, int> g_smem_attr;         // (fn, device) -> max dyn smem set
+
+int elem_size(int dtype) { return dtype == kF32 ? 4 : 2; }
+bool valid_dtype(int dtype) { return dtype == kF32 || dtype == kF16 || dtype == kBF16; }
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+int device_info(DeviceInfo* out, int* dev_out) {
+  int dev = 0;
+  CC1D_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return CC1D_ERR_INVALID;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_dev_ready[dev]) {
+    int sms = 0;
+    CC1D_TRY_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    void* st = nullptr;
+    CC1D_TRY_CUDA(cudaGetSymbolAddress(&st, g_status_word));
+    g_dev[dev].sms = sms;
+    g_dev[dev].status = static_cast<unsigned*>(st);
+    g_dev_ready[dev] = true;
+  }
+  *out = g_dev[dev];
+  *dev_out = dev;
+  return CC1D_OK;
+}
+
+// CTAs of `k` that fit on one SM with k.smem bytes of dynamic shared memory. The function's
+// dynamic shared memory limit is raised to `max_smem` once per device.
+int occupancy(const KernelInfo& k, int max_smem, int dev, int* occ) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  const auto key = std::make_tuple(k.fn, dev, k.smem);
+  auto it = g_occupancy.find(key);
+  if (it != g_occupancy.end()) {
+    *occ = it->second;
+    return CC1D_OK;
+  }
+  const auto akey = std::make_pair(k.fn, dev);
+  auto at = g_smem_attr.find(akey);
+  if (at == g_smem_attr.end() || at->second < max_smem) {
+    CC1D_TRY_CUDA(cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem));
+    g_smem_attr[akey] = max_smem;
+  }
+  int n = 0;
+  CC1D_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k.fn, k.threads, k.smem));
+  if (n < 1) return CC1D_ERR_UNSUPPORTED;
+  g_occupancy[key] = n;
+  *occ = n;
+  return CC1D_OK;
+}
+
+int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_encode == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    CC1D_TRY_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || p == nullptr) return cuda_fail(cudaErrorSymbolNotFound);
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  *fn = g_encode;
+  return CC1D_OK;
+}
+
+// Whether a (B, T, D) channels-last tensor at `ptr` with batch/time strides (in elements) can be
+// read by the TMA kernels: 16-byte aligned base and strides, and rows of out/dx (D elements)
+// that are whole 16-byte vectors.
+bool tma_layout_ok(const void* ptr, int64_t sb, int64_t st, int64_t B, int64_t D, int es) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return false;
+  if (st <= 0 || (st * es) % 16 != 0) return false;
+  if (B > 1 && (sb <= 0 || (sb * es) % 16 != 0)) return false;
+  return (D * es) % 16 == 0;
+}
+
+// 3-D tensor map over a (B, T, D) channels-last tensor, as dims (D, T, B), box (box_d, box_t, 1).
+// Rows outside [0, T) and channels outside [0, D) read as zero.
+bool encode_3d(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t T, int64_t D, int64_t sb,
+               int64_t st, int box_d, int box_t) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  if (tensor_map_encoder(&enc) != CC1D_OK) return false;
+  const int es = elem_size(dtype);
+  const CUtensorMapDataType dt = dtype == kF32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : dtype == kF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(T), static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(st * es),
+                                 static_cast<cuuint64_t>(B > 1 ? sb * es : T * st * es)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_d), static_cast<cuuint32_t>(box_t), 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+KernelInfo fwd_tma_for(int dtype, int W, bool seq, bool silu) {
+  if (dtype == kBF16) return fwd_tma_info<__nv_bfloat16>(W, seq, silu);
+  if (dtype == kF16) return fwd_tma_info<__half>(W, seq, silu);
+  return fwd_tma_info<float>(W, seq, silu);
+}
+KernelInfo bwd_tma_for(int dtype, int W, bool seq, bool silu) {
+  if (dtype == kBF16) return bwd_tma_info<__nv_bfloat16>(W, seq, silu);
+  if (dtype == kF16) return bwd_tma_info<__half>(W, seq, silu);
+  return bwd_tma_info<float>(W, seq, silu);
+}
+KernelInfo fwd_generic_for(int dtype, int W) {
+  if (dtype == kBF16) return fwd_generic_info<__nv_bfloat16>(W);
+  if (dtype == kF16) return fwd_generic_info<__half>(W);
+  return fwd_generic_info<float>(W);
+}
+KernelInfo bwd_generic_for(int dtype, int W) {
+  if (dtype == kBF16) return bwd_generic_info<__nv_bfloat16>(W);
+  if (dtype == kF16) return bwd_generic_info<__half>(W);
+  return bwd_generic_info<float>(W);
+}
+
+int launch_fill(void* dst, int dst_dtype, const void* src, int src_dtype, int64_t n, int sms, cudaStream_t stream) {
+  if (n <= 0) return CC1D_OK;
+  const int blocks = static_cast<int>(std::min<int64_t>(cdiv(n, 256), static_cast<int64_t>(sms) * 8));
+  cc1d_fill_kernel<<<blocks, 256, 0, stream>>>(dst, dst_dtype, src, src_dtype, n);
+  CC1D_TRY_CUDA(cudaGetLastError());
+  return CC1D_OK;
+}
+
+int check_sizes(int64_t B, int64_t T, int64_t D, int64_t W) {
+  if (B < 0 || T < 0 || D < 0 || W < 2) return CC1D_ERR_INVALID;
+  if (B >= (int64_t(1) << 31) || T >= (int64_t(1) << 31) || D >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+  if (B * cdiv(T, 64) >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+  if (W > kGenericMaxWidth) return CC1D_ERR_UNSUPPORTED;
+  return CC1D_OK;
+}
+
+// Launch plan of the backward: which kernel, how many CTAs, how many partial rows.
+struct BwdPlan {
+  bool tma = false;
+  KernelInfo k;
+  int max_smem = 0;
+  int P = 0;      // partial rows (CTAs per channel block)
+  int n_blk = 0;  // channel blocks
+  int n_tt = 0;   // time tiles per batch row
+  int64_t grid = 0;
+  int64_t ws_bytes = 0;
+};
+
+int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t syb, int64_t syt, int64_t B, int64_t T,
+             int64_t D, int64_t W, int x_dtype, bool seq, bool silu, const DeviceInfo& di, int dev, BwdPlan* pl) {
+  const int es = elem_size(x_dtype);
+  pl->tma = W <= 8 && tma_layout_ok(x, sxb, sxt, B, D, es) && tma_layout_ok(dy, syb, syt, B, D, es);
+  int occ = 0;
+  if (pl->tma) {
+    pl->k = bwd_tma_for(x_dtype, static_cast<int>(W), seq, silu);
+    pl->max_smem = pl->k.smem;
+    // The partial count must not depend on seq_idx (the workspace query does not see it): size the
+    // grid by the lower occupancy of the two variants.
+    const KernelInfo k0 = bwd_tma_for(x_dtype, static_cast<int>(W), false, silu);
+    const KernelInfo k1 = bwd_tma_for(x_dtype, static_cast<int>(W), true, silu);
+    int o0 = 0, o1 = 0;
+    CC1D_TRY(occupancy(k0, k0.smem, dev, &o0));
+    CC1D_TRY(occupancy(k1, k1.smem, dev, &o1));
+    occ = std::min(o0, o1);
+  } else {
+    pl->k = bwd_generic_for(x_dtype, static_cast<int>(W));
+    pl->max_smem = generic_bwd_smem(kGenericMaxWidth);
+    CC1D_TRY(occupancy(pl->k, pl->max_smem, dev, &occ));
+  }
+  pl->n_blk = static_cast<int>(cdiv(D, pl->k.d_tile));
+  pl->n_tt = static_cast<int>(cdiv(T, pl->k.t_tile));
+  const int64_t M = B * pl->n_tt;
+  const int64_t cap = static_cast<int64_t>(di.sms) * occ;
+  pl->P = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(M, cap / pl->n_blk)));
+  pl->grid = static_cast<int64_t>(pl->P) * pl->n_blk;
+  if (pl->grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+  pl->ws_bytes = static_cast<int64_t>(pl->P) * (W + 1) * D * 4;
+  return CC1D_OK;
+}
+
+}  // namespace
+}  // namespace cc1d
+
+using namespace cc1d;
+
+extern "C" {
+
+int cc1d_abi_version(void) { return 1; }
+
+const char* cc1d_error_string(int code) {
+  switch (code) {
+    case CC1D_OK: return "success";
+    case CC1D_ERR_INVALID: return "invalid argument (size, stride, dtype code or missing pointer)";
+    case CC1D_ERR_UNSUPPORTED: return "unsupported width (the largest supported width is 256)";
+    case CC1D_ERR_WORKSPACE: return "workspace smaller than cc1d_bwd_workspace_bytes()";
+    case CC1D_ERR_CUDA: return "CUDA call failed (see cc1d_last_cuda_error())";
+    default: return "unknown error";
+  }
+}
+
+int cc1d_last_cuda_error(void) { return t_last_cuda_error; }
+
+int cc1d_status(uint32_t* status, int clear) {
+  DeviceInfo di;
+  int dev = 0;
+  CC1D_TRY(device_info(&di, &dev));
+  CC1D_TRY_CUDA(cudaDeviceSynchronize());
+  unsigned v = 0;
+  CC1D_TRY_CUDA(cudaMemcpy(&v, di.status, sizeof(v), cudaMemcpyDeviceToHost));
+  if (clear) CC1D_TRY_CUDA(cudaMemset(di.status, 0, sizeof(unsigned)));
+  if (status) *status = v;
+  return CC1D_OK;
+}
+
+int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* weight, const void* bias,
+             const void* initial_states, const int32_t* seq_idx, void* out, void* final_states, int64_t batch,
+             int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype, int bias_dtype,
+             int init_dtype, int silu, void* stream_) {
+  if (!valid_dtype(x_dtype) || !valid_dtype(weight_dtype) || (bias && !valid_dtype(bias_dtype)) ||
+      (initial_states && !valid_dtype(init_dtype)))
+    return CC1D_ERR_INVALID;
+  CC1D_TRY(check_sizes(batch, seqlen, dim, width));
+  if (batch == 0 || dim == 0) return CC1D_OK;
+  const int64_t B = batch, T = seqlen, D = dim, W = width, PAD = W - 1;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DeviceInfo di;
+  int dev = 0;
+  CC1D_TRY(device_info(&di, &dev));
+  if (T == 0) {  // final_states = initial_states, or zero
+    if (final_states) CC1D_TRY(launch_fill(final_states, x_dtype, initial_states, init_dtype, B * PAD * D, di.sms, stream));
+    return CC1D_OK;
+  }
+  if (!x || !weight || !out) return CC1D_ERR_INVALID;
+
+  const int es = elem_size(x_dtype);
+  if (W <= 8 && tma_layout_ok(x, stride_x_batch, stride_x_time, B, D, es)) {
+    const KernelInfo k = fwd_tma_for(x_dtype, static_cast<int>(W), seq_idx != nullptr, silu != 0);
+    FwdParams p{};
+    if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, k.d_tile,
+                  k.t_tile + static_cast<int>(PAD))) {
+      int occ = 0;
+      CC1D_TRY(occupancy(k, k.smem, dev, &occ));
+      p.x = x, p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
+      p.out = out, p.final_states = final_states, p.status = di.status;
+      p.sxb = stride_x_batch, p.sxt = stride_x_time;
+      p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D);
+      p.n_tt = static_cast<int>(cdiv(T, k.t_tile));
+      p.n_db = static_cast<int>(cdiv(D, k.d_tile));
+      p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
+      const int64_t M = B * p.n_tt;
+      const int64_t cap = static_cast<int64_t>(di.sms) * occ;
+      const int64_t P = std::max<int64_t>(1, std::min<int64_t>(M, cap / p.n_db));
+      const int64_t grid = P * p.n_db;
+      if (grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+      void* args[] = {&p};
+      CC1D_TRY_CUDA(cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(grid)), dim3(k.threads), args, k.smem, stream));
+      return CC1D_OK;
+    }
+  }
+  // Generic path.
+  const KernelInfo k = fwd_generic_for(x_dtype, static_cast<int>(W));
+  int occ = 0;
+  CC1D_TRY(occupancy(k, generic_fwd_smem(kGenericMaxWidth), dev, &occ));
+  GenericParams g{};
+  g.x = x, g.weight = weight, g.bias = bias, g.init = initial_states, g.seq = seq_idx;
+  g.out = out, g.final_states = final_states, g.status = di.status;
+  g.sxb = stride_x_batch, g.sxt = stride_x_time;
+  g.B = static_cast<int>(B), g.T = static_cast<int>(T), g.D = static_cast<int>(D), g.W = static_cast<int>(W);
+  g.n_tt = static_cast<int>(cdiv(T, GT));
+  g.n_dc = static_cast<int>(cdiv(D, GC));
+  g.w_dtype = weight_dtype, g.b_dtype = bias_dtype, g.init_dtype = init_dtype, g.silu = silu != 0;
+  const int64_t grid = B * g.n_tt * g.n_dc;
+  if (grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+  void* args[] = {&g};
+  CC1D_TRY_CUDA(cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(grid)), dim3(k.threads), args, k.smem, stream));
+  return CC1D_OK;
+}
+
+int64_t cc1d_bwd_workspace_bytes(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* dout,
+                                 int64_t stride_dout_batch, int64_t stride_dout_time, int64_t batch, int64_t seqlen,
+                                 int64_t dim, int64_t width, int x_dtype) {
+  if (!valid_dtype(x_dtype) || check_sizes(batch, seqlen, dim, width) != CC1D_OK) return -1;
+  if (batch == 0 || dim == 0 || seqlen == 0) return 0;
+  DeviceInfo di;
+  int dev = 0;
+  if (device_info(&di, &dev) != CC1D_OK) return -1;
+  BwdPlan pl;
+  if (plan_bwd(x, stride_x_batch, stride_x_time, dout, stride_dout_batch, stride_dout_time, batch, seqlen, dim, width,
+               x_dtype, false, false, di, dev, &pl) != CC1D_OK)
+    return -1;
+  return pl.ws_bytes;
+}
+
+int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* weight, const void* bias,
+             const void* initial_states, const int32_t* seq_idx, const void* dout, int64_t stride_dout_batch,
+             int64_t stride_dout_time, const void* dfinal_states, void* dx, void* dweight, void* dbias, void* dinit,
+             float* grad_f32, void* workspace, int64_t workspace_bytes, int64_t batch, int64_t seqlen, int64_t dim,
+             int64_t width, int x_dtype, int weight_dtype, int bias_dtype, int init_dtype, int silu, void* stream_) {
+  if (!valid_dtype(x_dtype) || !valid_dtype(weight_dtype) || (bias && !valid_dtype(bias_dtype)) ||
+      (initial_states && !valid_dtype(init_dtype)))
+    return CC1D_ERR_INVALID;
+  if (dinit != nullptr && initial_states == nullptr) return CC1D_ERR_INVALID;
+  if (grad_f32 == nullptr && dweight == nullptr) return CC1D_ERR_INVALID;
+  CC1D_TRY(check_sizes(batch, seqlen, dim, width));
+  if (batch == 0 || dim == 0) return CC1D_OK;
+  const int64_t B = batch, T = seqlen, D = dim, W = width, PAD = W - 1;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DeviceInfo di;
+  int dev = 0;
+  CC1D_TRY(device_info(&di, &dev));
+  if (T == 0) {  // dinit = dfinal (or zero); no output rows, so dweight = dbias = 0
+    if (dinit) CC1D_TRY(launch_fill(dinit, init_dtype, dfinal_states, x_dtype, B * PAD * D, di.sms, stream));
+    if (grad_f32) {
+      CC1D_TRY(launch_fill(grad_f32, kF32, nullptr, kF32, (W + 1) * D, di.sms, stream));
+    } else {
+      CC1D_TRY(launch_fill(dweight, weight_dtype, nullptr, kF32, W * D, di.sms, stream));
+      if (bias && dbias) CC1D_TRY(launch_fill(dbias, bias_dtype, nullptr, kF32, D, di.sms, stream));
+    }
+    return CC1D_OK;
+  }
+  if (!x || !weight || !dout || !dx) return CC1D_ERR_INVALID;
+
+  BwdPlan pl;
+  CC1D_TRY(plan_bwd(x, stride_x_batch, stride_x_time, dout, stride_dout_batch, stride_dout_time, B, T, D, W, x_dtype,
+                    seq_idx != nullptr, silu != 0, di, dev, &pl));
+  if (workspace == nullptr || workspace_bytes < pl.ws_bytes) return CC1D_ERR_WORKSPACE;
+  float* partials = static_cast<float*>(workspace);
+
+  bool launched = false;
+  if (pl.tma) {
+    BwdParams p{};
+    const int PADi = static_cast<int>(PAD);
+    if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, pl.k.d_tile, pl.k.t_tile + 2 * PADi) &&
+        encode_3d(&p.tmap_dy, dout, x_dtype, B, T, D, stride_dout_batch, stride_dout_time, pl.k.d_tile,
+                  pl.k.t_tile + PADi)) {
+      int occ = 0;
+      CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
+      p.x = x, p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
+      p.dfinal = dfinal_states, p.dx = dx, p.dinit = dinit, p.partials = partials, p.status = di.status;
+      p.sxb = stride_x_batch, p.sxt = stride_x_time;
+      p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D);
+      p.n_tt = pl.n_tt, p.n_db = pl.n_blk;
+      p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
+      void* args[] = {&p};
+      CC1D_TRY_CUDA(
+          cudaLaunchKernel(pl.k.fn, dim3(static_cast<unsigned>(pl.grid)), dim3(pl.k.threads), args, pl.k.smem, stream));
+      launched = true;
+    }
+  }
+  if (!launched) {
+    // The tensor maps could not be encoded: re-plan on the generic path, whose partial count is
+    // never larger than the TMA path's, so the workspace still suffices.
+    if (pl.tma) {
+      const int64_t ws_tma = pl.ws_bytes;
+      pl.tma = false;
+      pl.k = bwd_generic_for(x_dtype, static_cast<int>(W));
+      pl.max_smem = generic_bwd_smem(kGenericMaxWidth);
+      int occ = 0;
+      CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
+      pl.n_blk = static_cast<int>(cdiv(D, pl.k.d_tile));
+      pl.n_tt = static_cast<int>(cdiv(T, pl.k.t_tile));
+      const int64_t M = B * pl.n_tt;
+      const int64_t cap = static_cast<int64_t>(di.sms) * occ;
+      const int64_t pmax = std::max<int64_t>(1, ws_tma / ((W + 1) * D * 4));
+      pl.P = static_cast<int>(std::max<int64_t>(1, std::min({M, cap / pl.n_blk, pmax})));
+      pl.grid = static_cast<int64_t>(pl.P) * pl.n_blk;
+    }
+    int occ = 0;
+    CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
+    GenericParams g{};
+    g.x = x, g.weight = weight, g.bias = bias, g.init = initial_states, g.seq = seq_idx;
+    g.dy = dout, g.dfinal = dfinal_states, g.dx = dx, g.dinit = dinit, g.partials = partials, g.status = di.status;
+    g.sxb = stride_x_batch, g.sxt = stride_x_time, g.syb = stride_dout_batch, g.syt = stride_dout_time;
+    g.B = static_cast<int>(B), g.T = static_cast<int>(T), g.D = static_cast<int>(D), g.W = static_cast<int>(W);
+    g.n_tt = pl.n_tt, g.n_dc = pl.n_blk;
+    g.w_dtype = weight_dtype, g.b_dtype = bias_dtype, g.init_dtype = init_dtype, g.silu = silu != 0;
+    void* args[] = {&g};
+    CC1D_TRY_CUDA(
+        cudaLaunchKernel(pl.k.fn, dim3(static_cast<unsigned>(pl.grid)), dim3(pl.k.threads), args, pl.k.smem, stream));
+  }
+
+  // Second stage: fixed-order sum over the P partial rows.
+  const int64_t N = (W + 1) * D;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(cdiv(N, 256), static_cast<int64_t>(di.sms) * 8)));
+  cc1d_reduce_partials_kernel<<<blocks, 256, 0, stream>>>(partials, pl.P, static_cast<int>(D), static_cast<int>(W),
+                                                          dweight, weight_dtype, bias ? dbias : nullptr, bias_dtype,
+                                                          grad_f32, bias != nullptr);
+  CC1D_TRY_CUDA(cudaGetLastError());
+  return CC1D_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,24 @@
+// Internal: tables of the compiled kernel variants, one translation unit per element type.
+#pragma once
+
+#include "cc1d_generic_kernels.cuh"
+#include "cc1d_tma_kernels.cuh"
+
+namespace cc1d {
+
+struct KernelInfo {
+  const void* fn = nullptr;  // __global__ function
+  int smem = 0;              // dynamic shared memory bytes
+  int threads = 0;           // block size
+  int d_tile = 0;            // channels per CTA tile
+  int t_tile = 0;            // time rows per CTA tile
+};
+
+// TMA path, widths 2..8; fn is null for widths outside that range.
+template <typename T> KernelInfo fwd_tma_info(int W, bool seq, bool silu);
+template <typename T> KernelInfo bwd_tma_info(int W, bool seq, bool silu);
+// Generic path, any width up to kGenericMaxWidth.
+template <typename T> KernelInfo fwd_generic_info(int W);
+template <typename T> KernelInfo bwd_generic_info(int W);
+
+}  // namespace cc1d

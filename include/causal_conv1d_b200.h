@@ -1,0 +1,116 @@
+/*
+ * C ABI of the B200 (sm_100a) causal depthwise conv1d library, libcausal_conv1d_b200.so.
+ *
+ *   out[b, t, d] = act(bias[d] + sum_k weight[d, k] * x[b, t - (W - 1) + k, d])
+ *
+ * over channels-last inputs x (B, T, D). Rows t < 0 read initial_states (B, W-1, D) or zero;
+ * seq_idx (B, T) int32 packs several sequences per row (taps never cross a sequence boundary and
+ * rows with a negative id are padding whose output is 0); act is identity or SiLU.
+ *
+ * These entry points replace the kernel launches of the reference implementation,
+ * jxiong21029/causal-conv1d-triton, causal_conv1d_triton/causal_conv1d.py, one for one. The
+ * argument lists carry what those launches pass (device pointers, the (B, T, D, W) sizes, the
+ * batch/time strides of x and dout in elements, the presence flags as null/non-null pointers)
+ * plus the element types the Triton JIT would read off the tensors and the CUDA stream that
+ * torch's current stream supplies there.
+ *
+ * Conventions for every entry point:
+ *  - All pointers are device pointers on the current CUDA device; the work is enqueued on
+ *    `stream` (a cudaStream_t; NULL is the legacy default stream). Nothing is allocated, nothing
+ *    synchronises the host, so the calls can be captured in a CUDA graph.
+ *  - The channel stride of x and dout is 1. out, dx, final_states, dinit, initial_states and
+ *    dfinal_states are contiguous. weight is (D, W) row-major, bias is (D).
+ *  - Element type codes: CC1D_F32, CC1D_F16, CC1D_BF16. out, final_states, dx and
+ *    dfinal_states have the type of x; dinit has the type of initial_states; dweight and dbias
+ *    have the types of weight and bias.
+ *  - Return value 0 on success, else one of CC1D_ERR_*; cc1d_error_string() describes it.
+ */
+#ifndef CAUSAL_CONV1D_B200_H_
+#define CAUSAL_CONV1D_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { CC1D_F32 = 0, CC1D_F16 = 1, CC1D_BF16 = 2 };
+
+enum {
+  CC1D_OK = 0,
+  CC1D_ERR_INVALID = 1,     /* bad size, stride, dtype code or missing required pointer */
+  CC1D_ERR_UNSUPPORTED = 2, /* width above the largest supported (256) */
+  CC1D_ERR_WORKSPACE = 3,   /* workspace smaller than cc1d_bwd_workspace_bytes() */
+  CC1D_ERR_CUDA = 4         /* a CUDA runtime/driver call failed; see cc1d_last_cuda_error() */
+};
+
+/* Interface version of this header; bumped on any signature change. */
+int cc1d_abi_version(void);
+
+/*
+ * Forward. Replaces the `_fwd_kernel[grid](...)` launch of `_fwd`, causal_conv1d.py:446-471,
+ * together with `_fwd`'s T == 0 case (:437-444: final_states = initial_states, or zero).
+ *   x               (B, T, D) at strides (stride_x_batch, stride_x_time, 1), type x_dtype
+ *   weight          (D, W), type weight_dtype;   bias (D) or NULL, type bias_dtype
+ *   initial_states  (B, W-1, D) or NULL, type init_dtype
+ *   seq_idx         (B, T) int32 or NULL
+ *   out             (B, T, D) contiguous, type x_dtype
+ *   final_states    (B, W-1, D) contiguous or NULL: the last W-1 rows of concat(initial_states, x)
+ *   silu            0 = no activation, 1 = SiLU
+ */
+int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* weight,
+             const void* bias, const void* initial_states, const int32_t* seq_idx, void* out,
+             void* final_states, int64_t batch, int64_t seqlen, int64_t dim, int64_t width,
+             int x_dtype, int weight_dtype, int bias_dtype, int init_dtype, int silu,
+             void* stream);
+
+/*
+ * Size in bytes of the fp32 workspace cc1d_bwd needs for its per-CTA weight/bias partial sums
+ * (the `partials` buffer that `_bwd` allocates, causal_conv1d.py:493). Depends on the sizes, the
+ * element type, the strides and 16-byte alignment of x and dout, and the current device.
+ */
+int64_t cc1d_bwd_workspace_bytes(const void* x, int64_t stride_x_batch, int64_t stride_x_time,
+                                 const void* dout, int64_t stride_dout_batch,
+                                 int64_t stride_dout_time, int64_t batch, int64_t seqlen,
+                                 int64_t dim, int64_t width, int x_dtype);
+
+/*
+ * Backward. Replaces the `_bwd_kernel` and `_reduce_partials_kernel` launches of `_bwd`,
+ * causal_conv1d.py:491-540, and `_bwd`'s T == 0 case (:480-489).
+ *   dout            (B, T, D) at strides (stride_dout_batch, stride_dout_time, 1), type x_dtype
+ *   dfinal_states   (B, W-1, D) or NULL, type x_dtype
+ *   dx              (B, T, D) contiguous, type x_dtype
+ *   dinit           (B, W-1, D) or NULL (requires initial_states), type init_dtype
+ *   dweight, dbias  written in weight_dtype / bias_dtype (dbias only when bias is given) ...
+ *   grad_f32        ... unless grad_f32 is non-NULL: then the fp32 vector
+ *                   [dweight (D, W) row-major, dbias (D)] of D*(W+1) floats is written there
+ *                   instead (dbias part zero without bias), ready for a cross-GPU all-reduce.
+ *   workspace       device buffer of at least cc1d_bwd_workspace_bytes(...) bytes.
+ * The weight/bias gradients are deterministic: a fixed-order sum of per-CTA partials.
+ */
+int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* weight,
+             const void* bias, const void* initial_states, const int32_t* seq_idx,
+             const void* dout, int64_t stride_dout_batch, int64_t stride_dout_time,
+             const void* dfinal_states, void* dx, void* dweight, void* dbias, void* dinit,
+             float* grad_f32, void* workspace, int64_t workspace_bytes, int64_t batch,
+             int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype,
+             int bias_dtype, int init_dtype, int silu, void* stream);
+
+/*
+ * Reads the device status word of the current device after synchronising it, and clears it when
+ * `clear` is non-zero. Bit 0 set: a kernel gave up waiting on one of its pipeline barriers
+ * (bounded at one second) and returned early, so its outputs are incomplete.
+ */
+int cc1d_status(uint32_t* status, int clear);
+
+/* Human-readable text for a CC1D_ERR_* code. */
+const char* cc1d_error_string(int code);
+
+/* The cudaError_t of the last failed CUDA call made by this library on the calling thread. */
+int cc1d_last_cuda_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAUSAL_CONV1D_B200_H_ */

@@ -1,0 +1,90 @@
+"""CPU-side checks of the C-ABI library and of the host logic (no GPU needed).
+
+- libcausal_conv1d_b200.so loads on a machine without a GPU and exports every function that
+  include/causal_conv1d_b200.h declares, with the signatures the ctypes binding uses.
+- The error codes and strings are stable.
+- causal_conv1d_fn raises the reference's errors for bad arguments before touching a device
+  (causal_conv1d_triton/causal_conv1d.py:605-611).
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "causal_conv1d_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(cc1d_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_abi():
+    names = declared_functions()
+    for n in ["cc1d_fwd", "cc1d_bwd", "cc1d_bwd_workspace_bytes", "cc1d_status",
+              "cc1d_error_string", "cc1d_last_cuda_error", "cc1d_abi_version"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    from causal_conv1d_b200 import _native
+
+    lib = ctypes.CDLL(_native.LIB_PATH)
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+        assert name in _native.SIGNATURES, f"{name} has no ctypes signature in _native"
+
+
+def test_abi_version_and_error_strings():
+    from causal_conv1d_b200 import _native
+
+    assert _native.lib.cc1d_abi_version() == 1
+    assert _native.lib.cc1d_error_string(0) == b"success"
+    for code in (1, 2, 3, 4):
+        assert len(_native.lib.cc1d_error_string(code)) > 5
+    assert _native.lib.cc1d_error_string(99) == b"unknown error"
+
+
+def test_invalid_sizes_rejected_without_device_work():
+    """Argument checks run before any CUDA call."""
+    from causal_conv1d_b200 import _native
+
+    lib = _native.lib
+    # width 1 is invalid, width 257 unsupported, negative sizes invalid, bad dtype code invalid
+    assert lib.cc1d_bwd_workspace_bytes(None, 0, 0, None, 0, 0, 1, 8, 8, 1, 2) == -1
+    assert lib.cc1d_bwd_workspace_bytes(None, 0, 0, None, 0, 0, 1, 8, 8, 257, 2) == -1
+    assert lib.cc1d_bwd_workspace_bytes(None, 0, 0, None, 0, 0, -1, 8, 8, 4, 2) == -1
+    assert lib.cc1d_bwd_workspace_bytes(None, 0, 0, None, 0, 0, 1, 8, 8, 4, 7) == -1
+    # empty inputs need no workspace
+    assert lib.cc1d_bwd_workspace_bytes(None, 0, 0, None, 0, 0, 0, 8, 8, 4, 2) == 0
+    rc = lib.cc1d_fwd(None, 0, 0, None, None, None, None, None, None, 1, 8, 8, 300,
+                      2, 0, 0, 0, 1, None)
+    assert rc == _native.CC1D_ERR_UNSUPPORTED
+    rc = lib.cc1d_fwd(None, 0, 0, None, None, None, None, None, None, 1, 8, 8, 4,
+                      9, 0, 0, 0, 1, None)
+    assert rc == _native.CC1D_ERR_INVALID
+
+
+def test_api_errors_match_reference():
+    from causal_conv1d_b200 import causal_conv1d_fn
+
+    x = torch.randn(2, 8, 4)
+    w = torch.randn(4, 3)
+    with pytest.raises(NotImplementedError):
+        causal_conv1d_fn(x, w, activation="relu")
+    with pytest.raises(AssertionError):
+        causal_conv1d_fn(x, w, seq_idx=torch.zeros(2, 8, dtype=torch.int32),
+                         return_final_states=True)
+    with pytest.raises(AssertionError):
+        causal_conv1d_fn(x, w, final_states_out=torch.empty(2, 2, 4))
+    with pytest.raises(AssertionError):  # weight must be (dim, width)
+        causal_conv1d_fn(x, torch.randn(5, 3))
+    with pytest.raises(AssertionError):  # width >= 2
+        causal_conv1d_fn(x, torch.randn(4, 1))
+    with pytest.raises(AssertionError):  # x must be on a CUDA device
+        causal_conv1d_fn(x, w)
