@@ -50,18 +50,23 @@ def _stale(target, deps) -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> str:
-    """Compiles every .cu under csrc/ for sm_100a and links the shared library; returns its path."""
-    os.makedirs(BUILD, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False,
+          defines: tuple = (), lib_path: str = LIB, build_dir: str = BUILD) -> str:
+    """Compiles every .cu under csrc/ for sm_100a and links the shared library; returns its path.
+
+    `defines` (e.g. ("CC1D_BWD_LAG=1",)) override the kernels' compile-time tuning constants; use
+    them with a separate `lib_path` and `build_dir`."""
+    os.makedirs(build_dir, exist_ok=True)
     nvcc = _nvcc()
     headers = _headers()
     srcs = sources()
-    objs = [os.path.join(BUILD, os.path.basename(s)[:-3] + ".o") for s in srcs]
+    objs = [os.path.join(build_dir, os.path.basename(s)[:-3] + ".o") for s in srcs]
+    dflags = [f"-D{d}" for d in defines]
     todo = [(s, o) for s, o in zip(srcs, objs) if force or ptxas_verbose or _stale(o, [s] + headers)]
 
     def compile_one(so):
         s, o = so
-        cmd = [nvcc] + NVCC_FLAGS + (["-Xptxas", "-v"] if ptxas_verbose else []) + ["-c", s, "-o", o]
+        cmd = [nvcc] + NVCC_FLAGS + dflags + (["-Xptxas", "-v"] if ptxas_verbose else []) + ["-c", s, "-o", o]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
@@ -74,14 +79,14 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
             for s, err in ex.map(compile_one, todo):
                 if ptxas_verbose and err:
                     print(f"== {os.path.basename(s)}\n{err}", flush=True)
-    if force or todo or _stale(LIB, objs):
-        cmd = [nvcc] + ARCH + ["-shared", "-o", LIB] + objs
+    if force or todo or _stale(lib_path, objs):
+        cmd = [nvcc] + ARCH + ["-shared", "-o", lib_path] + objs
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    return LIB
+    return lib_path
 
 
 if __name__ == "__main__":

@@ -48,6 +48,17 @@ struct TileCfg {
   static_assert(R >= PAD, "only row group 0 of the first tile reads rows t < 0");
 };
 
+// Backward schedule knobs (see the step loop of cc1d_bwd_tma_kernel).
+#ifndef CC1D_BWD_LAG
+#define CC1D_BWD_LAG 0
+#endif
+#ifndef CC1D_BWD_DX_FAR_FIRST
+#define CC1D_BWD_DX_FAR_FIRST 0
+#endif
+#ifndef CC1D_BWD_BIAS_FIRST
+#define CC1D_BWD_BIAS_FIRST 0
+#endif
+
 constexpr int kSmemAlign = 128;
 constexpr int kBarBytes = 128;  // full[] and empty[] barriers, at most 8 stages each
 
@@ -58,7 +69,10 @@ struct FwdLayout {
   static constexpr int XBYTES = XROWS * C::ROW_BYTES;
   static constexpr int SEQ_BYTES = SEQ ? (XROWS * 4 + 127) / 128 * 128 : 0;
   static constexpr int STAGE_BYTES = XBYTES + SEQ_BYTES;
-  static constexpr int STAGES = 4;
+  // CTAs per SM the stages and registers are sized for: 4 x 3 stages up to W = 4, 3 x 4 stages
+  // for wider windows (which need more registers per thread).
+  static constexpr int STAGES = W <= 4 ? 3 : 4;
+  static constexpr int MIN_CTAS = W <= 4 ? 4 : 3;
   static constexpr int SMEM_BYTES = kSmemAlign + kBarBytes + STAGES * STAGE_BYTES;
 };
 
@@ -71,9 +85,11 @@ struct BwdLayout {
   static constexpr int YBYTES = YROWS * C::ROW_BYTES;
   static constexpr int SEQ_BYTES = SEQ ? (XROWS * 4 + 127) / 128 * 128 : 0;
   static constexpr int STAGE_BYTES = XBYTES + YBYTES + SEQ_BYTES;
-  // Three stages when two CTAs still fit in the SM's 228 KB (each CTA also reserves 1 KB).
-  static constexpr int STAGES =
-      2 * (kSmemAlign + kBarBytes + 3 * STAGE_BYTES + 1024) <= 228 * 1024 ? 3 : 2;
+  // Two stages per CTA: up to W = 4 three CTAs (12 consumer warps) per SM fit in its 228 KB
+  // (each CTA also reserves 1 KB), which hides more latency than a third stage would; wider
+  // windows need more registers per thread and run two CTAs per SM.
+  static constexpr int STAGES = 2;
+  static constexpr int MIN_CTAS = W <= 4 ? 3 : 2;
   static constexpr int SMEM_BYTES = kSmemAlign + kBarBytes + STAGES * STAGE_BYTES;
   static constexpr int RED_BYTES = 4 * (W + 1) * C::D_TILE * 4;  // CTA-level dweight/dbias sum
   static_assert(RED_BYTES <= STAGES * STAGE_BYTES, "reduction buffer reuses the stages");
@@ -153,7 +169,7 @@ __device__ __forceinline__ void load_state_row(const void* base, int dtype, int6
 // Forward
 // =============================================================================================
 template <typename T, int W, bool SEQ, bool SILU>
-__global__ void __launch_bounds__(TileCfg<T, W>::THREADS, 3)
+__global__ void __launch_bounds__(TileCfg<T, W>::THREADS, FwdLayout<T, W, SEQ>::MIN_CTAS)
     cc1d_fwd_tma_kernel(const __grid_constant__ FwdParams p) {
   using C = TileCfg<T, W>;
   using L = FwdLayout<T, W, SEQ>;
@@ -282,7 +298,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::THREADS, 3)
       }
       if constexpr (SILU) {
 #pragma unroll
-        for (int i2 = 0; i2 < NP; ++i2) z[i2] = fmul2(z[i2], sigmoid2<FAST>(z[i2]));
+        for (int i2 = 0; i2 < NP; ++i2) z[i2] = silu2<FAST>(z[i2]);
       }
       if (dvalid && ts + r < p.T) store_vec<T, CPT>(orow + r * D, z);
 #pragma unroll
@@ -325,7 +341,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::THREADS, 3)
 // forward's order (causal_conv1d.py:274-288); dx[t] = sum_j w[PAD-j] dz[t+j] masked to the same
 // sequence (:290-296) plus dfinal_states (:297-302).
 template <typename T, int W, bool SEQ, bool SILU>
-__global__ void __launch_bounds__(TileCfg<T, W>::THREADS, 2)
+__global__ void __launch_bounds__(TileCfg<T, W>::THREADS, BwdLayout<T, W, SEQ>::MIN_CTAS)
     cc1d_bwd_tma_kernel(const __grid_constant__ BwdParams p) {
   using C = TileCfg<T, W>;
   using L = BwdLayout<T, W, SEQ>;
@@ -424,53 +440,60 @@ __global__ void __launch_bounds__(TileCfg<T, W>::THREADS, 2)
     const int ts = t0 + rb;
     const bool init_rows = p.init != nullptr && ts == 0;
 
-    // Before the step at t: xs[k] = x[t - PAD + 1 + k], dzs[j] = dz[t + 1 + j].
-    float2 xs[PAD][NP], dzs[PAD][NP];
-#pragma unroll
-    for (int k = 0; k < PAD; ++k) {
-      load_vec<T, CPT>(xt + (rb + R + PAD + k) * DT, xs[k]);
-#pragma unroll
-      for (int i2 = 0; i2 < NP; ++i2) dzs[k][i2] = make_float2(0.f, 0.f);
-    }
+    // Step s (0 <= s < NS) handles row t = top - s, walking backwards in time; steps s < PAD are
+    // the halo rows after this thread's own rows, which only provide dz. x rows are indexed from
+    // the top as xr[i] = x[top - i]; the window of step s is x[t - PAD + k] = xr[s + PAD - k].
+    // Each step is split into part A (load x and dy, recompute z, form dz) and part B (dx,
+    // dweight, dbias of an own row), and part B of step s is issued after part A of step s + LAG
+    // so that the independent A chains of later rows overlap the B chains of earlier ones.
+    constexpr int NS = R + PAD;
+    constexpr int NX = R + 2 * PAD;
+    constexpr int LAG = CC1D_BWD_LAG;
+    const int top_lt = rb + R + PAD - 1;  // t - t0 of step 0
+    float2 xr[NX][NP];
+    float2 dzr[NS][NP];
 
-#pragma unroll
-    for (int step = 0; step < R + PAD; ++step) {
-      const int lt = rb + R + PAD - 1 - step;  // t - t0
-      const int t = t0 + lt;
-      // win[k] = x[t - PAD + k]
-      float2 win[PAD + 1][NP];
-      if (step >= R && init_rows) {
+    auto load_x = [&](int i) {
+      // global row top - i; local smem row rb + R + 2 PAD - 1 - i; init row R + 2 PAD - 1 - i
+      if (i >= R + PAD && init_rows) {
         if (dvalid) {
-          load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * PAD + lt, p.D, d, win[0]);
+          load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * PAD + (R + 2 * PAD - 1 - i), p.D, d, xr[i]);
         } else {
 #pragma unroll
-          for (int i2 = 0; i2 < NP; ++i2) win[0][i2] = make_float2(0.f, 0.f);
+          for (int i2 = 0; i2 < NP; ++i2) xr[i][i2] = make_float2(0.f, 0.f);
         }
       } else {
-        load_vec<T, CPT>(xt + lt * DT, win[0]);
+        load_vec<T, CPT>(xt + (rb + R + 2 * PAD - 1 - i) * DT, xr[i]);
       }
+    };
+
+    auto part_a = [&](int s_, auto tail) {
+      constexpr bool TAIL = decltype(tail)::value;
+      const int lt = top_lt - s_;
+      const int t = t0 + lt;
+      if (s_ == 0) {
 #pragma unroll
-      for (int k = 1; k <= PAD; ++k)
-#pragma unroll
-        for (int i2 = 0; i2 < NP; ++i2) win[k][i2] = xs[k - 1][i2];
+        for (int i = 0; i < PAD; ++i) load_x(i);
+      }
+      load_x(s_ + PAD);
       float2 dz[NP];
       load_vec<T, CPT>(yt + lt * DT, dz);
       const int seq_t = SEQ ? sq[lt + PAD] : 0;
-
       if constexpr (SILU) {
         float2 z[NP];
 #pragma unroll
-        for (int i2 = 0; i2 < NP; ++i2) z[i2] = fmul2(w[PAD][i2], win[PAD][i2]);
+        for (int i2 = 0; i2 < NP; ++i2)
+          z[i2] = CC1D_BWD_BIAS_FIRST ? ffma2(w[PAD][i2], xr[s_][i2], bv[i2]) : fmul2(w[PAD][i2], xr[s_][i2]);
 #pragma unroll
         for (int k = 0; k < PAD; ++k) {
           if (!SEQ || sq[lt + k] == seq_t) {
 #pragma unroll
-            for (int i2 = 0; i2 < NP; ++i2) z[i2] = ffma2(w[k][i2], win[k][i2], z[i2]);
+            for (int i2 = 0; i2 < NP; ++i2) z[i2] = ffma2(w[k][i2], xr[s_ + PAD - k][i2], z[i2]);
           }
         }
 #pragma unroll
         for (int i2 = 0; i2 < NP; ++i2) {
-          z[i2] = fadd2(z[i2], bv[i2]);
+          if (!CC1D_BWD_BIAS_FIRST) z[i2] = fadd2(z[i2], bv[i2]);
           const float2 sg = sigmoid2<FAST>(z[i2]);
           const float2 one = make_float2(1.f, 1.f);
           const float2 oms = fadd2(one, make_float2(-sg.x, -sg.y));
@@ -478,60 +501,96 @@ __global__ void __launch_bounds__(TileCfg<T, W>::THREADS, 2)
           dz[i2] = fmul2(fmul2(dz[i2], sg), ffma2(z[i2], oms, one));
         }
       }
-      if ((SEQ && seq_t < 0) || t >= T_) {
+      if ((SEQ && seq_t < 0) || (TAIL && t >= T_)) {
 #pragma unroll
         for (int i2 = 0; i2 < NP; ++i2) dz[i2] = make_float2(0.f, 0.f);
       }
-
-      if (step >= PAD) {
-        // Own row t: dx[t] = w[PAD] dz[t] + sum_j w[PAD - j] dz[t + j], masked to the same sequence.
-        float2 g[NP];
 #pragma unroll
-        for (int i2 = 0; i2 < NP; ++i2) g[i2] = fmul2(w[PAD][i2], dz[i2]);
+      for (int i2 = 0; i2 < NP; ++i2) dzr[s_][i2] = dz[i2];
+    };
+
+    auto part_b = [&](int s_, auto tail) {
+      constexpr bool TAIL = decltype(tail)::value;
+      const int lt = top_lt - s_;
+      const int t = t0 + lt;
+      const int seq_t = SEQ ? sq[lt + PAD] : 0;
+      // dx[t] = w[PAD] dz[t] + sum_j w[PAD - j] dz[t + j] (dz[t + j] is step s - j), masked to the
+      // same sequence (causal_conv1d.py:290-296).
+      float2 g[NP];
+      if (CC1D_BWD_DX_FAR_FIRST) {
+#pragma unroll
+        for (int i2 = 0; i2 < NP; ++i2) g[i2] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = PAD; j >= 1; --j) {
+          if (!SEQ || sq[lt + PAD + j] == seq_t) {
+#pragma unroll
+            for (int i2 = 0; i2 < NP; ++i2) g[i2] = ffma2(w[PAD - j][i2], dzr[s_ - j][i2], g[i2]);
+          }
+        }
+#pragma unroll
+        for (int i2 = 0; i2 < NP; ++i2) g[i2] = ffma2(w[PAD][i2], dzr[s_][i2], g[i2]);
+      } else {
+#pragma unroll
+        for (int i2 = 0; i2 < NP; ++i2) g[i2] = fmul2(w[PAD][i2], dzr[s_][i2]);
 #pragma unroll
         for (int j = 1; j <= PAD; ++j) {
           if (!SEQ || sq[lt + PAD + j] == seq_t) {
 #pragma unroll
-            for (int i2 = 0; i2 < NP; ++i2) g[i2] = ffma2(w[PAD - j][i2], dzs[j - 1][i2], g[i2]);
+            for (int i2 = 0; i2 < NP; ++i2) g[i2] = ffma2(w[PAD - j][i2], dzr[s_ - j][i2], g[i2]);
           }
-        }
-        if (p.dfinal != nullptr && dvalid) {
-          const int f = t - (T_ - PAD);
-          if (f >= 0 && f < PAD) {
-            float2 v[NP];
-            load_state_row<NP>(p.dfinal, sizeof(T) == 4 ? kF32 : (std::is_same_v<T, __nv_bfloat16> ? kBF16 : kF16),
-                               static_cast<int64_t>(b) * PAD + f, p.D, d, v);
-#pragma unroll
-            for (int i2 = 0; i2 < NP; ++i2) g[i2] = fadd2(g[i2], v[i2]);
-          }
-        }
-        if (dvalid && t < T_) store_vec<T, CPT>(static_cast<T*>(p.dx) + (static_cast<int64_t>(b) * T_ + t) * D + d, g);
-        // dweight / dbias partial sums (causal_conv1d.py:313-321).
-#pragma unroll
-        for (int k = 0; k < PAD; ++k) {
-          if (!SEQ || sq[lt + k] == seq_t) {
-#pragma unroll
-            for (int i2 = 0; i2 < NP; ++i2) dw[k][i2] = ffma2(dz[i2], win[k][i2], dw[k][i2]);
-          }
-        }
-#pragma unroll
-        for (int i2 = 0; i2 < NP; ++i2) {
-          dw[PAD][i2] = ffma2(dz[i2], win[PAD][i2], dw[PAD][i2]);
-          dbs[i2] = fadd2(dbs[i2], dz[i2]);
         }
       }
-      // Shift the windows one row back in time.
+      if (TAIL && p.dfinal != nullptr && dvalid) {
+        const int f = t - (T_ - PAD);
+        if (f >= 0 && f < PAD) {
+          float2 v[NP];
+          load_state_row<NP>(p.dfinal, sizeof(T) == 4 ? kF32 : (std::is_same_v<T, __nv_bfloat16> ? kBF16 : kF16),
+                             static_cast<int64_t>(b) * PAD + f, p.D, d, v);
 #pragma unroll
-      for (int k = 0; k < PAD; ++k)
+          for (int i2 = 0; i2 < NP; ++i2) g[i2] = fadd2(g[i2], v[i2]);
+        }
+      }
+      if (!TAIL || (dvalid && t < T_))
+        store_vec<T, CPT>(static_cast<T*>(p.dx) + (static_cast<int64_t>(b) * T_ + t) * D + d, g);
+      // dweight / dbias partial sums (causal_conv1d.py:313-321).
 #pragma unroll
-        for (int i2 = 0; i2 < NP; ++i2) xs[k][i2] = win[k][i2];
+      for (int k = 0; k < PAD; ++k) {
+        if (!SEQ || sq[lt + k] == seq_t) {
 #pragma unroll
-      for (int j = PAD - 1; j > 0; --j)
+          for (int i2 = 0; i2 < NP; ++i2) dw[k][i2] = ffma2(dzr[s_][i2], xr[s_ + PAD - k][i2], dw[k][i2]);
+        }
+      }
 #pragma unroll
-        for (int i2 = 0; i2 < NP; ++i2) dzs[j][i2] = dzs[j - 1][i2];
+      for (int i2 = 0; i2 < NP; ++i2) {
+        dw[PAD][i2] = ffma2(dzr[s_][i2], xr[s_][i2], dw[PAD][i2]);
+        dbs[i2] = fadd2(dbs[i2], dzr[s_][i2]);
+      }
+    };
+
+    // With SiLU (compute-bound), interior tiles (every row of the window inside [0, T), no
+    // final-state rows, every channel in range) run a copy of the loop without any per-row bounds
+    // or final-state checks. Without it the kernel is bandwidth-bound and one general copy of the
+    // loop is faster.
+    const bool tail = !SILU || !dvalid || t0 + C::T_TILE + PAD > T_ || (p.dfinal != nullptr && t0 + C::T_TILE > T_ - PAD);
+    if (SILU && !tail) {
 #pragma unroll
-      for (int i2 = 0; i2 < NP; ++i2) dzs[0][i2] = dz[i2];
+      for (int u = 0; u < NS + LAG; ++u) {
+        if (u < NS) part_a(u, std::false_type{});
+        if (u - LAG >= PAD && u - LAG < NS) part_b(u - LAG, std::false_type{});
+      }
+    } else {
+#pragma unroll
+      for (int u = 0; u < NS + LAG; ++u) {
+        if (u < NS) part_a(u, std::true_type{});
+        if (u - LAG >= PAD && u - LAG < NS) part_b(u - LAG, std::true_type{});
+      }
     }
+    // dz of rows ts .. ts + PAD - 1, for the dinitial_states rows below.
+    float2 dzs[PAD][NP];
+#pragma unroll
+    for (int j = 0; j < PAD; ++j)
+#pragma unroll
+      for (int i2 = 0; i2 < NP; ++i2) dzs[j][i2] = dzr[NS - 1 - j][i2];
     // dinitial_states: rows t = -1 .. -PAD, where dz = 0 (causal_conv1d.py:224-225, 306-311).
     if (p.dinit != nullptr && ts == 0 && dvalid) {
       const int seq0 = SEQ ? sq[PAD - 1] : 0;  // rows t < 0 carry seq_idx[b, 0]
