@@ -22,6 +22,7 @@ CC1D_ERR_INVALID = 1
 CC1D_ERR_UNSUPPORTED = 2
 CC1D_ERR_WORKSPACE = 3
 CC1D_ERR_CUDA = 4
+CC1D_ERR_SCRATCH_LIMIT = 5
 
 # Every symbol the header declares, with its ctypes signature.
 _P, _I64, _I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
@@ -33,6 +34,8 @@ SIGNATURES = {
                                  _I64),
     "cc1d_bwd": ([_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P,
                   _P, _I64, _I64, _I64, _I64, _I64, _I, _I, _I, _I, _I, _P], _I),
+    "cc1d_bwd_noalloc": ([_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P,
+                          _I64, _I64, _I64, _I64, _I, _I, _I, _I, _I, _P], _I),
     "cc1d_status": ([ctypes.POINTER(ctypes.c_uint32), _I], _I),
     "cc1d_error_string": ([_I], ctypes.c_char_p),
     "cc1d_last_cuda_error": ([], _I),

@@ -240,6 +240,8 @@ const char* cc1d_error_string(int code) {
     case CC1D_ERR_UNSUPPORTED: return "unsupported width (the largest supported width is 256)";
     case CC1D_ERR_WORKSPACE: return "workspace smaller than cc1d_bwd_workspace_bytes()";
     case CC1D_ERR_CUDA: return "CUDA call failed (see cc1d_last_cuda_error())";
+    case CC1D_ERR_SCRATCH_LIMIT:
+      return "backward needs more scratch than cc1d_bwd_noalloc's fixed 8 MiB buffer; call cc1d_bwd with a workspace";
     default: return "unknown error";
   }
 }
@@ -436,3 +438,74 @@ int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// cc1d_bwd_noalloc: the backward for callers that cannot allocate device memory.
+//
+// cc1d_bwd needs a caller-provided device workspace for its per-CTA weight/bias partial sums.
+// Some callers have no way to provide one: an inference or training runtime that carves all of
+// device memory into its own arena at start-up and must not call cudaMalloc afterwards (the call
+// can fail or fragment the arena), a latency-critical path where cudaMalloc/cudaFree may
+// synchronise the whole device, or host code that reaches this library only through its C ABI
+// (an FFI binding) with no device allocator of its own. For them the partial sums live in a
+// fixed array in the library's own device memory instead, sized for ordinary shapes.
+//
+// Limits and behaviour:
+//  - The array holds kNoAllocScratchBytes (8 MiB). A call whose plan needs more (the same number
+//    cc1d_bwd_workspace_bytes returns) is rejected with CC1D_ERR_SCRATCH_LIMIT before any device
+//    work; use cc1d_bwd with a workspace for it.
+//  - The array exists once per GPU that loads the library, and stays allocated until the process
+//    exits.
+//  - Nothing is allocated here: no cudaMalloc, cudaFree or allocating library routine. The
+//    kernels write every partial they later read, so no part of the array has to start at zero
+//    and nothing is cleared between calls; the array keeps the last call's partial sums.
+//  - Every call on a device shares the one array, so calls that overlap on the GPU (different
+//    streams, no ordering between them) race on it and give wrong gradients. Order them (one
+//    stream, or events).
+//  - The first call on each device looks up the array's device address with
+//    cudaGetSymbolAddress, with that device current; make that first call before any stream
+//    capture begins.
+// ---------------------------------------------------------------------------------------------
+namespace cc1d {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  CC1D_TRY_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return CC1D_ERR_INVALID;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    CC1D_TRY_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return CC1D_OK;
+}
+
+}  // namespace
+}  // namespace cc1d
+
+extern "C" int cc1d_bwd_noalloc(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* weight,
+                                const void* bias, const void* initial_states, const int32_t* seq_idx, const void* dout,
+                                int64_t stride_dout_batch, int64_t stride_dout_time, const void* dfinal_states,
+                                void* dx, void* dweight, void* dbias, void* dinit, float* grad_f32, int64_t batch,
+                                int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype,
+                                int bias_dtype, int init_dtype, int silu, void* stream) {
+  const int64_t need = cc1d_bwd_workspace_bytes(x, stride_x_batch, stride_x_time, dout, stride_dout_batch,
+                                                stride_dout_time, batch, seqlen, dim, width, x_dtype);
+  if (need < 0) return CC1D_ERR_INVALID;
+  if (static_cast<uint64_t>(need) > cc1d::kNoAllocScratchBytes) return CC1D_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  const int rc = cc1d::noalloc_scratch(&scratch);
+  if (rc != CC1D_OK) return rc;
+  return cc1d_bwd(x, stride_x_batch, stride_x_time, weight, bias, initial_states, seq_idx, dout, stride_dout_batch,
+                  stride_dout_time, dfinal_states, dx, dweight, dbias, dinit, grad_f32, scratch,
+                  static_cast<int64_t>(cc1d::kNoAllocScratchBytes), batch, seqlen, dim, width, x_dtype, weight_dtype,
+                  bias_dtype, init_dtype, silu, stream);
+}

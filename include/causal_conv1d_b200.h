@@ -16,8 +16,8 @@
  *
  * Conventions for every entry point:
  *  - All pointers are device pointers on the current CUDA device; the work is enqueued on
- *    `stream` (a cudaStream_t; NULL is the legacy default stream). Nothing is allocated, nothing
- *    synchronises the host, so the calls can be captured in a CUDA graph.
+ *    `stream` (a cudaStream_t; NULL is the legacy default stream). cc1d_fwd and cc1d_bwd allocate
+ *    nothing and never synchronise the host, so they can be captured in a CUDA graph.
  *  - The channel stride of x and dout is 1. out, dx, final_states, dinit, initial_states and
  *    dfinal_states are contiguous. weight is (D, W) row-major, bias is (D).
  *  - Element type codes: CC1D_F32, CC1D_F16, CC1D_BF16. out, final_states, dx and
@@ -41,7 +41,8 @@ enum {
   CC1D_ERR_INVALID = 1,     /* bad size, stride, dtype code or missing required pointer */
   CC1D_ERR_UNSUPPORTED = 2, /* width above the largest supported (256) */
   CC1D_ERR_WORKSPACE = 3,   /* workspace smaller than cc1d_bwd_workspace_bytes() */
-  CC1D_ERR_CUDA = 4         /* a CUDA runtime/driver call failed; see cc1d_last_cuda_error() */
+  CC1D_ERR_CUDA = 4,        /* a CUDA runtime/driver call failed; see cc1d_last_cuda_error() */
+  CC1D_ERR_SCRATCH_LIMIT = 5 /* cc1d_bwd_noalloc: problem needs more than its fixed scratch */
 };
 
 /* Interface version of this header; bumped on any signature change. */
@@ -95,6 +96,27 @@ int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
              float* grad_f32, void* workspace, int64_t workspace_bytes, int64_t batch,
              int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype,
              int bias_dtype, int init_dtype, int silu, void* stream);
+
+/*
+ * Backward without any device allocation, for callers that cannot allocate: runtimes that own all
+ * of device memory in a pre-planned arena and must not call cudaMalloc after start-up, paths where
+ * cudaMalloc/cudaFree could synchronise the device, and FFI callers with no device allocator. No
+ * counterpart in the reference (its `_bwd` allocates the partials with torch, causal_conv1d.py:493).
+ * Same arguments and results as cc1d_bwd, minus the workspace: the partial sums go to one fixed
+ * 8 MiB array in the library's device memory (per GPU that loads the library, held until the
+ * process exits). Problems whose cc1d_bwd_workspace_bytes() exceeds 8 MiB are rejected with
+ * CC1D_ERR_SCRATCH_LIMIT before any device work. All calls on a device share the array, so calls
+ * that overlap on the GPU race; order them on one stream. Nothing in the array must start at zero.
+ * The first call on each device looks up the array's address (cudaGetSymbolAddress) with that
+ * device current; make it before any stream capture.
+ */
+int cc1d_bwd_noalloc(const void* x, int64_t stride_x_batch, int64_t stride_x_time,
+                     const void* weight, const void* bias, const void* initial_states,
+                     const int32_t* seq_idx, const void* dout, int64_t stride_dout_batch,
+                     int64_t stride_dout_time, const void* dfinal_states, void* dx,
+                     void* dweight, void* dbias, void* dinit, float* grad_f32, int64_t batch,
+                     int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype,
+                     int bias_dtype, int init_dtype, int silu, void* stream);
 
 /*
  * Reads the device status word of the current device after synchronising it, and clears it when
