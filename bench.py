@@ -191,12 +191,13 @@ def run_reference_cpu(args):
     x, w, b, dy = make_inputs(B, T, D, W, bias_silu)
     rows = min(T, 2048)  # bounded sample per step: batch row 0, first 2048 time rows
     xs, dys = x[:1, :rows].float().numpy(), dy[:1, :rows].float().numpy()
-    cores = os.cpu_count()
     fb, bb = algo_bytes(1, rows, D, W)
 
+    threads = os.cpu_count()
+
     def step():
-        oracle.fwd(xs, w, b, None, None, silu=bias_silu)
-        oracle.bwd(xs, w, b, None, None, dys, None, False, silu=bias_silu)
+        oracle.fwd(xs, w, b, None, None, silu=bias_silu, nthreads=threads)
+        oracle.bwd(xs, w, b, None, None, dys, None, False, silu=bias_silu, nthreads=threads)
 
     for _ in range(args.warmup):
         step()
@@ -212,7 +213,7 @@ def run_reference_cpu(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "impl": "reference",
         "data": "synthetic, seed 0",
         "config": workload_config(args),
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -366,11 +367,12 @@ def main():
     line["e2e"] = e2e(args, dev, x_h, w_h, b_h, dy_h, bias_silu, world, dist)
 
     if rank == 0:
-        cores = torch.get_num_threads()
-        gbs, sample, _ = cpu_sample_gbs(w_h, b_h, x_h, dy_h, bias_silu, args.cpu_seconds, nthreads=0)
-        line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": os.cpu_count(),
-                                "kind": "port", "sample": sample,
-                                "torch_threads": cores}
+        if world == 1:  # the CPU baseline is measured at N = 1 only
+            threads = os.cpu_count()
+            gbs, sample, _ = cpu_sample_gbs(w_h, b_h, x_h, dy_h, bias_silu, args.cpu_seconds,
+                                            nthreads=threads)
+            line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": threads,
+                                    "kind": "port", "sample": sample}
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -379,6 +381,9 @@ def main():
 
 def e2e(args, dev, x_h, w_h, b_h, dy_h, bias_silu, world, dist):
     from causal_conv1d_b200 import causal_conv1d_fn
+    from causal_conv1d_b200.distributed import sharded_causal_conv1d_fn
+
+    fn = sharded_causal_conv1d_fn if world > 1 else causal_conv1d_fn
 
     xp, dyp = x_h.pin_memory(), dy_h.pin_memory()
     out_h = torch.empty_like(x_h).pin_memory()
@@ -395,11 +400,8 @@ def e2e(args, dev, x_h, w_h, b_h, dy_h, bias_silu, world, dist):
         w.grad = None
         if b is not None:
             b.grad = None
-        out = causal_conv1d_fn(x, w, b, activation="silu" if bias_silu else None)
+        out = fn(x, w, b, activation="silu" if bias_silu else None)
         out.backward(dy)
-        if world > 1:
-            g = torch.cat([w.grad.flatten()] + ([b.grad] if b is not None else []))
-            dist.all_reduce(g)
         out_h.copy_(out, non_blocking=True)
         dx_h.copy_(x.grad, non_blocking=True)
         dw_h.copy_(w.grad, non_blocking=True)

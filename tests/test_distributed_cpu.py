@@ -1,0 +1,114 @@
+"""Host logic of the batch-sharded data-parallel path, with gloo ranks on the CPU (no GPU).
+
+Each of 2 ranks takes its shard of the batch (shard_rows), computes its weight/bias gradient with
+the CPU oracle as the flat fp32 vector [dweight (D, W), dbias (D)] the backward kernel writes,
+all-reduces it (allreduce_flat_grad_) and splits it (split_flat_grad); the result must equal the
+oracle's gradient over the whole batch on every rank. A rank that raises leaves the others with an
+error from the process group instead of a hang.
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_shard_rows_cover_batch_exactly():
+    from causal_conv1d_b200.distributed import shard_rows
+
+    for batch in (1, 2, 7, 8, 64, 65):
+        for world in (1, 2, 3, 4, 8):
+            got = [shard_rows(batch, r, world) for r in range(world)]
+            rows = [i for s in got for i in range(s.start, s.stop)]
+            assert rows == list(range(batch))
+            sizes = [s.stop - s.start for s in got]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_rows(8, 2, 2)
+
+
+def test_split_flat_grad_layout():
+    from causal_conv1d_b200.distributed import flat_grad_size, split_flat_grad
+
+    D, W = 5, 3
+    flat = torch.arange(flat_grad_size(D, W), dtype=torch.float32)
+    dw, db = split_flat_grad(flat, D, W, torch.float32, torch.bfloat16)
+    assert dw.shape == (D, W) and dw[1, 2].item() == 5.0
+    assert db.dtype == torch.bfloat16 and db[0].item() == 15.0
+    dw2, db2 = split_flat_grad(flat, D, W, torch.float16, None)
+    assert dw2.dtype == torch.float16 and db2 is None
+
+
+def _worker(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import sys
+
+    sys.path[:0] = [p for p in os.environ["CC1D_TEST_PATHS"].split(os.pathsep)]
+    from causal_conv1d_b200.distributed import (allreduce_flat_grad_, flat_grad_size, shard_rows,
+                                                split_flat_grad)
+    from oracle import oracle
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    g = torch.Generator().manual_seed(0)
+    B, T, D, W = 5, 40, 24, 4
+    x = torch.randn(B, T, D, generator=g)
+    w = torch.randn(D, W, generator=g) * 0.5
+    b = torch.randn(D, generator=g) * 0.3
+    dy = torch.randn(B, T, D, generator=g)
+    sl = shard_rows(B, rank, world)
+    _, dw, db, _ = oracle.bwd(x[sl], w, b, None, None, dy[sl], None, False, silu=True)
+    flat = torch.from_numpy(np.concatenate([dw.reshape(-1), db]))
+    assert flat.numel() == flat_grad_size(D, W)
+    allreduce_flat_grad_(flat)
+    dweight, dbias = split_flat_grad(flat, D, W, torch.float32, torch.float32)
+    _, rdw, rdb, _ = oracle.bwd(x, w, b, None, None, dy, None, False, silu=True)
+    np.testing.assert_allclose(dweight.numpy(), rdw, rtol=1e-5, atol=1e-5 * np.abs(rdw).max())
+    np.testing.assert_allclose(dbias.numpy(), rdb, rtol=1e-5, atol=1e-5 * np.abs(rdb).max())
+    torch.save({"dw": dweight, "db": dbias}, os.path.join(result_dir, f"r{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def _paths():
+    import sys
+
+    return os.pathsep.join(p for p in sys.path if "repo" in p)
+
+
+def test_gloo_two_ranks_match_full_batch(tmp_path):
+    os.environ["CC1D_TEST_PATHS"] = _paths()
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    r0, r1 = torch.load(tmp_path / "r0.pt"), torch.load(tmp_path / "r1.pt")
+    assert torch.equal(r0["dw"], r1["dw"]) and torch.equal(r0["db"], r1["db"])
+
+
+def _failing_worker(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        raise RuntimeError("rank 1 fails before its all-reduce")
+    t = torch.ones(4)
+    try:
+        dist.all_reduce(t)
+    except Exception:
+        return  # the surviving rank sees an error, not a hang
+    raise AssertionError("all_reduce with a dead peer should have failed")
+
+
+def test_gloo_dead_rank_raises_instead_of_hanging():
+    with pytest.raises(Exception):
+        mp.spawn(_failing_worker, args=(2, _free_port()), nprocs=2, join=True)

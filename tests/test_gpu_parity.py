@@ -299,3 +299,23 @@ def test_no_grad_path_and_other_device_stream(cc):
         out = cc.causal_conv1d_fn(x, w, activation="silu")
     s.synchronize()
     assert torch.equal(out, ref)
+
+
+def test_sharded_fn_single_rank_matches_api(cc):
+    """Without a process group the data-parallel wrapper equals causal_conv1d_fn exactly."""
+    from causal_conv1d_b200.distributed import sharded_causal_conv1d_fn
+
+    g = torch.Generator().manual_seed(9)
+    x0 = torch.randn(2, 300, 256, generator=g).to(torch.bfloat16).to(DEV)
+    w0 = (torch.randn(256, 4, generator=g) * 0.5).to(DEV)
+    b0 = torch.randn(256, generator=g).to(DEV)
+    i0 = torch.randn(2, 3, 256, generator=g).to(torch.bfloat16).to(DEV)
+    dy = torch.randn(2, 300, 256, generator=g).to(torch.bfloat16).to(DEV)
+    res = []
+    for fn in (cc.causal_conv1d_fn, sharded_causal_conv1d_fn):
+        x, w, b, i = (t.clone().requires_grad_(True) for t in (x0, w0, b0, i0))
+        out = fn(x, w, b, initial_states=i, activation="silu")
+        out.backward(dy)
+        res.append([out, x.grad, w.grad, b.grad, i.grad])
+    for a, c in zip(*res):
+        assert torch.equal(a, c)
