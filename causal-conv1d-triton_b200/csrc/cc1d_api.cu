@@ -185,9 +185,10 @@ struct BwdPlan {
   bool tma = false;
   KernelInfo k;
   int max_smem = 0;
-  int P = 0;      // partial rows (CTAs per channel block)
-  int n_blk = 0;  // channel blocks
-  int n_tt = 0;   // time tiles per batch row
+  int P = 0;      // partial rows (CTAs per channel block / group)
+  int n_blk = 0;  // channel blocks (generic) or channel groups (TMA)
+  int n_tt = 0;   // generic: time tiles per batch row
+  int64_t rows_per_part = 0;  // TMA: flattened (batch, time) rows per CTA
   int64_t grid = 0;
   int64_t ws_bytes = 0;
 };
@@ -214,10 +215,20 @@ int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t sy
     CC1D_TRY(occupancy(pl->k, pl->max_smem, dev, &occ));
   }
   pl->n_blk = static_cast<int>(cdiv(D, pl->k.d_tile));
-  pl->n_tt = static_cast<int>(cdiv(T, pl->k.t_tile));
-  const int64_t M = B * pl->n_tt;
   const int64_t cap = static_cast<int64_t>(di.sms) * occ;
-  pl->P = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(M, cap / pl->n_blk)));
+  if (pl->tma) {
+    // One resident wave: P CTAs per channel group, each walking an equal stretch of the B*T rows
+    // (a multiple of the stage height).
+    const int64_t rows = B * T;
+    const int64_t rs = pl->k.t_tile;
+    const int64_t pmax = std::max<int64_t>(1, std::min<int64_t>(cdiv(rows, rs), cap / pl->n_blk));
+    pl->rows_per_part = cdiv(cdiv(rows, pmax), rs) * rs;
+    pl->P = static_cast<int>(cdiv(rows, pl->rows_per_part));
+  } else {
+    pl->n_tt = static_cast<int>(cdiv(T, pl->k.t_tile));
+    const int64_t M = B * pl->n_tt;
+    pl->P = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(M, cap / pl->n_blk)));
+  }
   pl->grid = static_cast<int64_t>(pl->P) * pl->n_blk;
   if (pl->grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
   pl->ws_bytes = static_cast<int64_t>(pl->P) * (W + 1) * D * 4;
@@ -376,18 +387,18 @@ int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
 
   bool launched = false;
   if (pl.tma) {
-    BwdParams p{};
+    BwdWalkParams p{};
     const int PADi = static_cast<int>(PAD);
-    if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, pl.k.d_tile, pl.k.t_tile + 2 * PADi) &&
-        encode_3d(&p.tmap_dy, dout, x_dtype, B, T, D, stride_dout_batch, stride_dout_time, pl.k.d_tile,
-                  pl.k.t_tile + PADi)) {
+    const int box_d = pl.k.d_tile / 4;  // one channel block per consumer warp
+    if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, box_d, pl.k.t_tile + PADi) &&
+        encode_3d(&p.tmap_dy, dout, x_dtype, B, T, D, stride_dout_batch, stride_dout_time, box_d, pl.k.t_tile)) {
       int occ = 0;
       CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
-      p.x = x, p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
+      p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
       p.dfinal = dfinal_states, p.dx = dx, p.dinit = dinit, p.partials = partials, p.status = di.status;
-      p.sxb = stride_x_batch, p.sxt = stride_x_time;
+      p.rows_per_part = pl.rows_per_part;
       p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D);
-      p.n_tt = pl.n_tt, p.n_db = pl.n_blk;
+      p.n_groups = pl.n_blk;
       p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
       void* args[] = {&p};
       CC1D_TRY_CUDA(
@@ -427,12 +438,22 @@ int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
         cudaLaunchKernel(pl.k.fn, dim3(static_cast<unsigned>(pl.grid)), dim3(pl.k.threads), args, pl.k.smem, stream));
   }
 
-  // Second stage: fixed-order sum over the P partial rows.
+  // Second stage: fixed-order sum over the P partial rows (32 column groups x 32 row slices per block).
   const int64_t N = (W + 1) * D;
-  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(cdiv(N, 256), static_cast<int64_t>(di.sms) * 8)));
-  cc1d_reduce_partials_kernel<<<blocks, 256, 0, stream>>>(partials, pl.P, static_cast<int>(D), static_cast<int>(W),
-                                                          dweight, weight_dtype, bias ? dbias : nullptr, bias_dtype,
-                                                          grad_f32, bias != nullptr);
+  const bool vec4 = N % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0;
+  const int64_t groups = vec4 ? N / 4 : N;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(cdiv(groups, kReduceCols), 65535)));
+  const int rthreads = kReduceCols * kReduceSlices;
+  if (vec4)
+    cc1d_reduce_partials_kernel<4><<<blocks, rthreads, 0, stream>>>(partials, pl.P, static_cast<int>(D),
+                                                                    static_cast<int>(W), dweight, weight_dtype,
+                                                                    bias ? dbias : nullptr, bias_dtype, grad_f32,
+                                                                    bias != nullptr);
+  else
+    cc1d_reduce_partials_kernel<1><<<blocks, rthreads, 0, stream>>>(partials, pl.P, static_cast<int>(D),
+                                                                    static_cast<int>(W), dweight, weight_dtype,
+                                                                    bias ? dbias : nullptr, bias_dtype, grad_f32,
+                                                                    bias != nullptr);
   CC1D_TRY_CUDA(cudaGetLastError());
   return CC1D_OK;
 }

@@ -1,0 +1,398 @@
+// TMA-pipelined sm_100a backward of the causal depthwise conv1d (widths 2..8):
+//
+//   dz[t]  = dout[t] * act'(z[t]),   z[t] = bias + sum_k w[k] x[t-(W-1)+k]    (recomputed)
+//   dx[t]  = sum_{j=0..W-1} w[W-1-j] dz[t+j]                                  (+ dfinal_states)
+//   dw[k] += dz[t] x[t-(W-1)+k],  db += dz[t]                                 (over all b, t)
+//
+// Work decomposition. A CTA owns a channel group of 4 x D_TILE channels (one 128-channel block of
+// bf16/fp16, or 64 of fp32, per consumer warp) and one contiguous stretch of L rows of the
+// flattened (batch, time) index, i.e. one or two contiguous time segments of batch rows. It walks
+// each segment backwards in time, 16 rows per pipeline stage, from W-1 rows past the segment's end
+// (the halo whose dz the segment's last dx rows need) down to the segment's first row, and then,
+// for the segment that starts at t = 0 when initial states need a gradient, to t = -(W-1). Because
+// the walk is continuous, every row's dz is computed once; only the W-1 halo rows per segment are
+// computed twice. The dz of the W-1 most recent rows, and all partial sums, stay in registers.
+//
+// Each CTA runs one producer warp, which issues per stage 4 TMA loads of x (rows a_lo-(W-1) ..
+// a_lo+15) and 4 of dout (rows a_lo .. a_lo+15) into a 2-stage mbarrier ring and writes the stage's
+// seq_idx window, and 4 consumer warps. Stages are aligned to the bottom of each segment, so the
+// last stage of a segment starts exactly at its first row; only the segment's top stage can be
+// partial. Consumer lanes own CPT consecutive channels (an 8-byte vector) and compute in fp32 pairs
+// with the sm_100 f32x2 instructions. A stage whose 16 rows all belong to the segment (no halo, no
+// initial-state rows, no final-state rows, channels in range) runs a copy of the step loop without
+// any per-row checks.
+//
+// Each warp owns distinct channels, so at the end each thread writes its dweight/dbias partials
+// for its channels straight to the (P, W+1, D) workspace (P = CTAs per channel group); a
+// fixed-order reduction over P follows (cc1d_reduce_kernels.cuh).
+//
+// Reference: jxiong21029/causal-conv1d-triton, causal_conv1d_triton/causal_conv1d.py,
+// `_bwd_kernel` :167-341 (per-element arithmetic and its order, seq_idx conventions, dinit rows).
+#pragma once
+
+#include "cc1d_tma_kernels.cuh"
+
+namespace cc1d {
+
+template <typename T, int W>
+struct BwdCfg {
+  static constexpr int ES = static_cast<int>(sizeof(T));
+  static constexpr int ROW_BYTES = 256;          // one channel block's row segment
+  static constexpr int D_TILE = ROW_BYTES / ES;  // channels per warp
+  static constexpr int CPT = 8 / ES;             // channels per lane
+  static constexpr int NP = CPT / 2;             // fp32 pairs per lane
+  static constexpr int WARPS = 4;                // consumer warps = channel blocks per CTA
+  static constexpr int THREADS = WARPS * 32 + 32;
+  static constexpr int DG = WARPS * D_TILE;      // channels per CTA
+  static constexpr int RS = 16;                  // rows per stage
+  static constexpr int PAD = W - 1;
+  static constexpr int XROWS = RS + PAD;         // x rows a_lo - PAD .. a_lo + RS - 1
+  static constexpr int SROWS = RS + 2 * PAD;     // seq rows a_lo - PAD .. a_lo + RS + PAD - 1
+  static constexpr int XBYTES = WARPS * XROWS * ROW_BYTES;
+  static constexpr int YBYTES = WARPS * RS * ROW_BYTES;
+  static constexpr int SEQ_BYTES = (SROWS * 4 + 127) / 128 * 128;
+  static constexpr int STAGE_BYTES = XBYTES + YBYTES + SEQ_BYTES;
+  static constexpr int STAGES = 2;
+  // CTAs per SM the registers are bounded for: three up to W = 4, two for wider windows.
+  static constexpr int MIN_CTAS = W <= 4 ? 3 : 2;
+  static constexpr int SMEM_BYTES = kSmemAlign + kBarBytes + STAGES * STAGE_BYTES;
+  static_assert(RS >= PAD, "dinit rows come from the last stage of a segment");
+};
+
+struct alignas(64) BwdWalkParams {
+  CUtensorMap tmap_x;   // x as (D, T, B), box (D_TILE, RS + PAD, 1)
+  CUtensorMap tmap_dy;  // dout as (D, T, B), box (D_TILE, RS, 1)
+  const void* weight;
+  const void* bias;
+  const void* init;     // (B, W-1, D) contiguous or null
+  const int32_t* seq;   // (B, T) or null (the SEQ variant only)
+  const void* dfinal;   // (B, W-1, D) contiguous, dtype of x, or null
+  void* dx;             // (B, T, D) contiguous
+  void* dinit;          // (B, W-1, D) contiguous, dtype of init, or null
+  float* partials;      // (P, W+1, D) fp32, P = gridDim.x / n_groups
+  unsigned* status;
+  int64_t rows_per_part;  // L, a multiple of RS
+  int B, T, D;
+  int n_groups;           // channel groups of DG channels
+  int w_dtype, b_dtype, init_dtype;
+};
+
+// The stages a CTA walks, in order: for each segment [s_lo, s_hi) of each batch row its stretch of
+// rows touches, the stages from the top (partial) one down to the one starting at s_lo. The
+// producer and the consumers run the same enumeration.
+template <int RS, int PAD>
+struct SegmentWalk {
+  int64_t r0, r1;  // flattened rows [r0, r1) of this CTA
+  int T;
+
+  template <typename F>
+  __device__ __forceinline__ void for_each_segment(F&& f) const {
+    if (r0 >= r1) return;
+    const int b_first = static_cast<int>(r0 / T), b_last = static_cast<int>((r1 - 1) / T);
+    for (int b = b_first; b <= b_last; ++b) {
+      const int64_t base = static_cast<int64_t>(b) * T;
+      const int s_lo = static_cast<int>(r0 > base ? r0 - base : 0);
+      const int s_hi = static_cast<int>(r1 - base < T ? r1 - base : T);
+      const int t_top = (s_hi + PAD < T ? s_hi + PAD : T) - 1;
+      const int n_st = (t_top - s_lo + RS) / RS;  // ceil((t_top - s_lo + 1) / RS)
+      f(b, s_lo, s_hi, t_top, n_st);
+    }
+  }
+};
+
+template <typename T, int W, bool SEQ, bool SILU>
+__global__ void __launch_bounds__(BwdCfg<T, W>::THREADS, BwdCfg<T, W>::MIN_CTAS)
+    cc1d_bwd_walk_kernel(const __grid_constant__ BwdWalkParams p) {
+  using C = BwdCfg<T, W>;
+  constexpr int PAD = C::PAD, RS = C::RS, CPT = C::CPT, NP = C::NP, S = C::STAGES;
+  constexpr int DT = C::D_TILE;
+  constexpr bool FAST = sizeof(T) == 2;
+  constexpr int XDT = sizeof(T) == 4 ? kF32 : (std::is_same_v<T, __nv_bfloat16> ? kBF16 : kF16);
+
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + (kSmemAlign - 1)) & ~uintptr_t(kSmemAlign - 1));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + S;
+  unsigned char* stage0 = smem + kBarBytes;
+
+  const int ng = p.n_groups;
+  const int g = blockIdx.x % ng;
+  const int part = blockIdx.x / ng;
+  const int T_ = p.T;
+  const int64_t D = p.D;
+  const int64_t total = static_cast<int64_t>(p.B) * T_;
+  SegmentWalk<RS, PAD> walk;
+  walk.r0 = static_cast<int64_t>(part) * p.rows_per_part;
+  walk.r1 = walk.r0 + p.rows_per_part < total ? walk.r0 + p.rows_per_part : total;
+  walk.T = T_;
+  // Channel blocks of this group that hold any channel < D.
+  const int nvb = min(C::WARPS, static_cast<int>((D - static_cast<int64_t>(g) * C::DG + DT - 1) / DT));
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 32);
+      mbar_init(&empty[s], C::WARPS);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == C::WARPS) {
+    // ---------------- producer warp ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&p.tmap_x);
+      prefetch_tensormap(&p.tmap_dy);
+    }
+    int i = 0;
+    bool ok = true;
+    walk.for_each_segment([&](int b, int s_lo, int, int, int n_st) {
+      for (int j = n_st - 1; j >= 0 && ok; --j, ++i) {
+        const int a_lo = s_lo + RS * j;  // processed top stage first: j = n_st - 1 .. 0
+        const int s = i % S;
+        if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, p.status)) {
+          ok = false;
+          break;
+        }
+        unsigned char* st = stage0 + s * C::STAGE_BYTES;
+        if (lane == 0) {
+          mbar_expect_tx(&full[s], static_cast<uint32_t>(nvb) * (C::XROWS + RS) * C::ROW_BYTES);
+          for (int k = 0; k < nvb; ++k) {
+            const int c0 = (g * C::WARPS + k) * DT;
+            tma_load_3d(st + k * C::XROWS * C::ROW_BYTES, &p.tmap_x, &full[s], c0, a_lo - PAD, b);
+            tma_load_3d(st + C::XBYTES + k * RS * C::ROW_BYTES, &p.tmap_dy, &full[s], c0, a_lo, b);
+          }
+        }
+        if constexpr (SEQ) {
+          int* sq = reinterpret_cast<int*>(st + C::XBYTES + C::YBYTES);
+          const int32_t* srow = p.seq + static_cast<int64_t>(b) * T_;
+          for (int r = lane; r < C::SROWS; r += 32) sq[r] = seq_at(srow, a_lo - PAD + r, T_, p.init != nullptr);
+        }
+        mbar_arrive(&full[s]);
+      }
+    });
+    // Every copy this CTA issued must have landed before the CTA may exit.
+    if (lane == 0)
+      for (int j = i > S ? i - S : 0; j < i; ++j) mbar_wait(&full[j % S], (j / S) & 1, p.status);
+    return;
+  }
+
+  // ---------------- consumer warps: warp = channel block ----------------
+  const int blk = warp;
+  const bool blk_valid = blk < nvb;
+  const int d = (g * C::WARPS + blk) * DT + lane * CPT;
+  const bool dvalid = d < p.D;
+  const bool has_init = p.init != nullptr;
+
+  float2 w[W][NP], bv[NP];
+  load_taps<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, w, bv);
+  float2 dw[W][NP], dbs[NP];
+#pragma unroll
+  for (int i2 = 0; i2 < NP; ++i2) {
+    dbs[i2] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < W; ++k) dw[k][i2] = make_float2(0.f, 0.f);
+  }
+
+  int i = 0;
+  bool ok = true;
+  walk.for_each_segment([&](int b, int s_lo, int s_hi, int t_top, int n_st) {
+    // dzs[j] = dz[a_hi + 1 + j]: the dz of the PAD rows above the current stage.
+    float2 dzs[PAD][NP];
+#pragma unroll
+    for (int j = 0; j < PAD; ++j)
+#pragma unroll
+      for (int i2 = 0; i2 < NP; ++i2) dzs[j][i2] = make_float2(0.f, 0.f);
+
+    for (int jst = n_st - 1; jst >= 0 && ok; --jst, ++i) {
+      const int s = i % S;
+      const int a_lo = s_lo + RS * jst;
+      const int a_hi = a_lo + RS - 1;
+      if (!mbar_wait(&full[s], (i / S) & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      const unsigned char* st = stage0 + s * C::STAGE_BYTES;
+      // x row q <-> global row a_lo - PAD + q; dy row q <-> a_lo + q; seq row q <-> a_lo - PAD + q.
+      const T* xt = reinterpret_cast<const T*>(st + blk * C::XROWS * C::ROW_BYTES) + lane * CPT;
+      const T* yt = reinterpret_cast<const T*>(st + C::XBYTES + blk * RS * C::ROW_BYTES) + lane * CPT;
+      const int* sq = reinterpret_cast<const int*>(st + C::XBYTES + C::YBYTES);
+
+      if (blk_valid) {
+        // Step s handles row t = a_hi - s. xr[i] = x[a_hi - i] (x row RS - 1 + PAD - i); the window
+        // of step s is x[t - PAD + k] = xr[s + PAD - k]. dzall[PAD + s] = dz of step s and
+        // dzall[PAD - 1 - j] = dzs[j], so dz[t + j] = dzall[PAD + s - j].
+        float2 xr[RS + PAD][NP];
+        float2 dzall[PAD + RS][NP];
+#pragma unroll
+        for (int j = 0; j < PAD; ++j)
+#pragma unroll
+          for (int i2 = 0; i2 < NP; ++i2) dzall[PAD - 1 - j][i2] = dzs[j][i2];
+
+        auto load_x = [&](int ix, auto general) {
+          constexpr bool GEN = decltype(general)::value;
+          const int q = RS - 1 + PAD - ix;
+          if (GEN && has_init && a_lo - PAD + q < 0) {
+            if (dvalid) {
+              load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * PAD + (a_lo + q), p.D, d, xr[ix]);
+            } else {
+#pragma unroll
+              for (int i2 = 0; i2 < NP; ++i2) xr[ix][i2] = make_float2(0.f, 0.f);
+            }
+          } else {
+            load_vec<T, CPT>(xt + q * DT, xr[ix]);
+          }
+        };
+
+        auto step = [&](int s_, auto general) {
+          constexpr bool GEN = decltype(general)::value;
+          const int t = a_hi - s_;
+          const int qs = RS - 1 - s_ + PAD;  // seq row of t
+          if (s_ == 0) {
+#pragma unroll
+            for (int ix = 0; ix < PAD; ++ix) load_x(ix, general);
+          }
+          load_x(s_ + PAD, general);
+          // Row classes (general stages only): above the walk (t > t_top: dz = 0), halo rows
+          // (s_hi <= t <= t_top: dz only), own rows.
+          const bool above = GEN && t > t_top;
+          const bool own = !GEN || t < s_hi;
+          float2 dz[NP];
+          load_vec<T, CPT>(yt + (RS - 1 - s_) * DT, dz);
+          const int seq_t = SEQ ? sq[qs] : 0;
+          if constexpr (SILU) {
+            float2 z[NP];
+#pragma unroll
+            for (int i2 = 0; i2 < NP; ++i2) z[i2] = fmul2(w[PAD][i2], xr[s_][i2]);
+#pragma unroll
+            for (int k = 0; k < PAD; ++k) {
+              if (!SEQ || sq[qs - PAD + k] == seq_t) {
+#pragma unroll
+                for (int i2 = 0; i2 < NP; ++i2) z[i2] = ffma2(w[k][i2], xr[s_ + PAD - k][i2], z[i2]);
+              }
+            }
+#pragma unroll
+            for (int i2 = 0; i2 < NP; ++i2) {
+              z[i2] = fadd2(z[i2], bv[i2]);
+              const float2 sg = sigmoid2<FAST>(z[i2]);
+              const float2 one = make_float2(1.f, 1.f);
+              const float2 oms = ffma2(sg, make_float2(-1.f, -1.f), one);
+              // dz = dy * sig * (1 + z * (1 - sig))   (causal_conv1d.py:285-286)
+              dz[i2] = fmul2(fmul2(dz[i2], sg), ffma2(z[i2], oms, one));
+            }
+          }
+          if ((SEQ && seq_t < 0) || above) {
+#pragma unroll
+            for (int i2 = 0; i2 < NP; ++i2) dz[i2] = make_float2(0.f, 0.f);
+          }
+#pragma unroll
+          for (int i2 = 0; i2 < NP; ++i2) dzall[PAD + s_][i2] = dz[i2];
+          if (!own) return;
+
+          // dx[t] = w[PAD] dz[t] + sum_j w[PAD - j] dz[t + j], masked to the same sequence
+          // (causal_conv1d.py:290-296), + dfinal_states (:297-302).
+          float2 gx[NP];
+#pragma unroll
+          for (int i2 = 0; i2 < NP; ++i2) gx[i2] = fmul2(w[PAD][i2], dz[i2]);
+#pragma unroll
+          for (int j = 1; j <= PAD; ++j) {
+            if (!SEQ || sq[qs + j] == seq_t) {
+#pragma unroll
+              for (int i2 = 0; i2 < NP; ++i2) gx[i2] = ffma2(w[PAD - j][i2], dzall[PAD + s_ - j][i2], gx[i2]);
+            }
+          }
+          if (GEN && p.dfinal != nullptr && dvalid) {
+            const int f = t - (T_ - PAD);
+            if (f >= 0) {
+              float2 v[NP];
+              load_state_row<NP>(p.dfinal, XDT, static_cast<int64_t>(b) * PAD + f, p.D, d, v);
+#pragma unroll
+              for (int i2 = 0; i2 < NP; ++i2) gx[i2] = fadd2(gx[i2], v[i2]);
+            }
+          }
+          if (!GEN || dvalid) store_vec<T, CPT>(static_cast<T*>(p.dx) + (static_cast<int64_t>(b) * T_ + t) * D + d, gx);
+          // dweight / dbias partial sums (causal_conv1d.py:313-321).
+#pragma unroll
+          for (int k = 0; k < PAD; ++k) {
+            if (!SEQ || sq[qs - PAD + k] == seq_t) {
+#pragma unroll
+              for (int i2 = 0; i2 < NP; ++i2) dw[k][i2] = ffma2(dz[i2], xr[s_ + PAD - k][i2], dw[k][i2]);
+            }
+          }
+#pragma unroll
+          for (int i2 = 0; i2 < NP; ++i2) {
+            dw[PAD][i2] = ffma2(dz[i2], xr[s_][i2], dw[PAD][i2]);
+            dbs[i2] = fadd2(dbs[i2], dz[i2]);
+          }
+        };
+
+        const bool interior = a_hi < s_hi && a_lo - PAD >= 0 && dvalid &&
+                              !(p.dfinal != nullptr && a_hi >= T_ - PAD);
+        if (interior) {
+#pragma unroll
+          for (int s_ = 0; s_ < RS; ++s_) step(s_, std::false_type{});
+        } else {
+#pragma unroll
+          for (int s_ = 0; s_ < RS; ++s_) step(s_, std::true_type{});
+        }
+        // Carry the dz of this stage's lowest PAD rows into the next stage.
+#pragma unroll
+        for (int j = 0; j < PAD; ++j)
+#pragma unroll
+          for (int i2 = 0; i2 < NP; ++i2) dzs[j][i2] = dzall[PAD + RS - 1 - j][i2];
+
+        // dinitial_states: rows t = -1 .. -PAD after the stage that starts at t = 0, where dz = 0
+        // (causal_conv1d.py:224-225, 306-311). dzs[j] = dz[j] here.
+        if (jst == 0 && s_lo == 0 && p.dinit != nullptr && dvalid) {
+          const int seq0 = SEQ ? sq[PAD - 1] : 0;  // rows t < 0 carry seq_idx[b, 0]
+#pragma unroll
+          for (int q = 1; q <= PAD; ++q) {
+            const int t = -q;
+            float2 gx[NP];
+#pragma unroll
+            for (int i2 = 0; i2 < NP; ++i2) gx[i2] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int j = q; j <= PAD; ++j) {  // dz[t + j] with t + j >= 0
+              if (!SEQ || sq[t + j + PAD] == seq0) {
+#pragma unroll
+                for (int i2 = 0; i2 < NP; ++i2) gx[i2] = ffma2(w[PAD - j][i2], dzs[j - q][i2], gx[i2]);
+              }
+            }
+            if (p.dfinal != nullptr) {
+              const int f = t - (T_ - PAD);
+              if (f >= 0) {
+                float2 v[NP];
+                load_state_row<NP>(p.dfinal, XDT, static_cast<int64_t>(b) * PAD + f, p.D, d, v);
+#pragma unroll
+                for (int i2 = 0; i2 < NP; ++i2) gx[i2] = fadd2(gx[i2], v[i2]);
+              }
+            }
+            const int64_t o = (static_cast<int64_t>(b) * PAD + t + PAD) * D + d;
+#pragma unroll
+            for (int i2 = 0; i2 < NP; ++i2) {
+              st_any(p.dinit, o + 2 * i2, p.init_dtype, gx[i2].x);
+              st_any(p.dinit, o + 2 * i2 + 1, p.init_dtype, gx[i2].y);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  });
+
+  // This thread's channels belong to this warp alone: write the partial sums directly.
+  if (dvalid) {
+    float* pp = p.partials + static_cast<int64_t>(part) * (W + 1) * D + d;
+#pragma unroll
+    for (int k = 0; k < W; ++k)
+#pragma unroll
+      for (int i2 = 0; i2 < NP; ++i2) *reinterpret_cast<float2*>(pp + k * D + 2 * i2) = dw[k][i2];
+#pragma unroll
+    for (int i2 = 0; i2 < NP; ++i2) *reinterpret_cast<float2*>(pp + W * D + 2 * i2) = dbs[i2];
+  }
+}
+
+}  // namespace cc1d

@@ -1,6 +1,7 @@
 // Internal: tables of the compiled kernel variants, one translation unit per element type.
 #pragma once
 
+#include "cc1d_bwd_kernel.cuh"
 #include "cc1d_generic_kernels.cuh"
 #include "cc1d_tma_kernels.cuh"
 
@@ -10,8 +11,8 @@ struct KernelInfo {
   const void* fn = nullptr;  // __global__ function
   int smem = 0;              // dynamic shared memory bytes
   int threads = 0;           // block size
-  int d_tile = 0;            // channels per CTA tile
-  int t_tile = 0;            // time rows per CTA tile
+  int d_tile = 0;            // channels per CTA tile (per CTA channel group for the TMA backward)
+  int t_tile = 0;            // time rows per CTA tile (per pipeline stage for the TMA backward)
 };
 
 // TMA path, widths 2..8; fn is null for widths outside that range.

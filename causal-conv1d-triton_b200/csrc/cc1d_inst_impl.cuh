@@ -15,9 +15,9 @@ KernelInfo fwd_tma_one() {
 }
 template <typename T, int W, bool SEQ, bool SILU>
 KernelInfo bwd_tma_one() {
-  using C = TileCfg<T, W>;
-  return {reinterpret_cast<const void*>(&cc1d_bwd_tma_kernel<T, W, SEQ, SILU>), BwdLayout<T, W, SEQ>::SMEM_BYTES,
-          C::THREADS, C::D_TILE, C::T_TILE};
+  using C = BwdCfg<T, W>;
+  return {reinterpret_cast<const void*>(&cc1d_bwd_walk_kernel<T, W, SEQ, SILU>), C::SMEM_BYTES, C::THREADS, C::DG,
+          C::RS};
 }
 template <typename T, int W>
 KernelInfo fwd_tma_w(bool seq, bool silu) {

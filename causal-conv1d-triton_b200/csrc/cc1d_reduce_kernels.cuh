@@ -10,37 +10,70 @@
 namespace cc1d {
 
 // Second stage of the dweight/dbias reduction (causal_conv1d.py:344-374): column n = k * D + d of
-// the (P, W+1, D) partials is summed over P in increasing P order, so the result does not depend
-// on scheduling. Writes dweight[d, k] (k < W) and dbias[d] (k == W) in their own dtypes, or, when
+// the (P, W+1, D) partials is summed over P in a fixed order (slice k of 32 sums rows k, k + 32, ...
+// in increasing order, then the 32 slice sums are added in order), so the result does not depend
+// on scheduling. All of a thread's loads are independent, so the whole buffer is in flight at once. Writes dweight[d, k] (k < W) and dbias[d] (k == W) in their own dtypes, or, when
 // grad_f32 is given, the fp32 vector [dweight (D, W) row-major, dbias (D)] instead (its dbias
 // part zero when there is no bias).
-__global__ void __launch_bounds__(256) cc1d_reduce_partials_kernel(const float* __restrict__ partials, int P, int D, int W,
-                                                                   void* dweight, int w_dtype, void* dbias, int b_dtype,
-                                                                   float* grad_f32, int has_bias) {
+constexpr int kReduceCols = 32;    // column groups per block
+constexpr int kReduceSlices = 32;  // partial rows are split over 32 warps: p = slice, slice + 32, ...
+
+__device__ __forceinline__ void reduce_store(int64_t n, float t, int D, int W, void* dweight, int w_dtype,
+                                             void* dbias, int b_dtype, float* grad_f32, int has_bias) {
+  const int k = static_cast<int>(n / D), d = static_cast<int>(n - static_cast<int64_t>(k) * D);
+  if (grad_f32 != nullptr) {
+    if (k < W)
+      grad_f32[static_cast<int64_t>(d) * W + k] = t;
+    else
+      grad_f32[static_cast<int64_t>(D) * W + d] = has_bias ? t : 0.0f;
+  } else if (k < W) {
+    st_any(dweight, static_cast<int64_t>(d) * W + k, w_dtype, t);
+  } else if (dbias != nullptr) {
+    st_any(dbias, d, b_dtype, t);
+  }
+}
+
+// VEC = 4: each thread sums 4 adjacent columns with 16-byte loads (requires N % 4 == 0 and a
+// 16-byte aligned buffer); VEC = 1: one column per thread.
+template <int VEC>
+__global__ void __launch_bounds__(kReduceCols * kReduceSlices)
+    cc1d_reduce_partials_kernel(const float* __restrict__ partials, int P, int D, int W, void* dweight, int w_dtype,
+                                void* dbias, int b_dtype, float* grad_f32, int has_bias) {
+  __shared__ float part_sums[kReduceSlices][kReduceCols][VEC];
   const int64_t N = static_cast<int64_t>(W + 1) * D;
-  for (int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; n < N;
-       n += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float s = 0.0f;
-    int q = 0;
-    for (; q + 8 <= P; q += 8) {
-      float v[8];
+  const int64_t NG = N / VEC;  // column groups
+  const int c = threadIdx.x % kReduceCols, sl = threadIdx.x / kReduceCols;
+  for (int64_t g0 = static_cast<int64_t>(blockIdx.x) * kReduceCols; g0 < NG;
+       g0 += static_cast<int64_t>(gridDim.x) * kReduceCols) {
+    const int64_t gi = g0 + c;
+    float s[VEC];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __ldg(partials + (q + u) * N + n);
+    for (int v = 0; v < VEC; ++v) s[v] = 0.0f;
+    if (gi < NG) {
+      const float* col = partials + gi * VEC;
+#pragma unroll 8
+      for (int q = sl; q < P; q += kReduceSlices) {
+        if constexpr (VEC == 4) {
+          const float4 x = __ldg(reinterpret_cast<const float4*>(col + static_cast<int64_t>(q) * N));
+          s[0] += x.x, s[1] += x.y, s[2] += x.z, s[3] += x.w;
+        } else {
+          s[0] += __ldg(col + static_cast<int64_t>(q) * N);
+        }
+      }
+    }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) s += v[u];
+    for (int v = 0; v < VEC; ++v) part_sums[sl][c][v] = s[v];
+    __syncthreads();
+    if (sl == 0 && gi < NG) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) {
+        float t = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kReduceSlices; ++k) t += part_sums[k][c][v];
+        reduce_store(gi * VEC + v, t, D, W, dweight, w_dtype, dbias, b_dtype, grad_f32, has_bias);
+      }
     }
-    for (; q < P; ++q) s += __ldg(partials + q * N + n);
-    const int k = static_cast<int>(n / D), d = static_cast<int>(n - static_cast<int64_t>(k) * D);
-    if (grad_f32 != nullptr) {
-      if (k < W)
-        grad_f32[static_cast<int64_t>(d) * W + k] = s;
-      else
-        grad_f32[static_cast<int64_t>(D) * W + d] = has_bias ? s : 0.0f;
-    } else if (k < W) {
-      st_any(dweight, static_cast<int64_t>(d) * W + k, w_dtype, s);
-    } else if (dbias != nullptr) {
-      st_any(dbias, d, b_dtype, s);
-    }
+    __syncthreads();
   }
 }
 
