@@ -47,10 +47,11 @@ METRIC = "fwd/bwd HBM GB/s (% of ~8 TB/s) and µs/call, bf16 D=1024 W=4"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 
-# Per-launch DRAM traffic (read + write bytes) of the backward kernel from one ncu capture of the
-# small case (B=8, T=8192, D=1024), scaled by units to this workload; see profiles/. None until
-# measured.
-BWD_DRAM_BYTES_PER_LAUNCH = None
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the backward kernel at
+# this workload (B=8, T=32768, D=1024, W=4, bias+SiLU), from the ncu launch list in
+# profiles/bwd_walk_kernel_cfg2.md; it scales with the B*T rows processed.
+BWD_DRAM_BYTES_PER_LAUNCH = 1090.6e6 + 510.0e6
+BWD_DRAM_ROWS = 8 * 32768
 
 
 def parse():
@@ -155,6 +156,21 @@ class ClockSampler:
             return {"unavailable": "no samples"}
         return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs), "samples": len(sms),
                 "reasons": sorted(reasons)}
+
+
+def same_size_copy_gbs(x, stream, reps=20):
+    """Read+write throughput of torch's device copy of a tensor the size of x: the copy rate this
+    workload's tensors can reach, a tighter ceiling than the 2 GiB copy of MEASURED_PEAKS.json."""
+    out = torch.empty_like(x)
+    for _ in range(3):
+        out.copy_(x)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        out.copy_(x)
+    e.record(stream)
+    torch.cuda.synchronize()
+    return 2 * x.numel() * x.element_size() * reps / (s.elapsed_time(e) * 1e-3) / 1e9
 
 
 def cpu_sample_gbs(w, b, x, dy, silu, seconds, nthreads=0, rows=None):
@@ -326,6 +342,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms, fwd_ms, bwd_ms = t.tolist()
 
+    copy_gbs = same_size_copy_gbs(x, stream)
     ms_step = total_ms / args.steps
     value = (fbytes + bbytes) * world / (ms_step * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
@@ -359,8 +376,10 @@ def main():
     line["roofline"] = {
         "bound": "hbm", "kernel": "cc1d_bwd_tma_kernel (+ reduce)", "achieved": bwd_gbs,
         "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak, "peak_source": f"{peak_kind} hbm_gbs",
-        "traffic": BWD_DRAM_BYTES_PER_LAUNCH * (B * T) / (8 * 8192) if BWD_DRAM_BYTES_PER_LAUNCH else None,
+        "traffic": BWD_DRAM_BYTES_PER_LAUNCH * (B * T) / BWD_DRAM_ROWS,
         "algorithmic_bytes": bbytes,
+        "copy_same_size_gbs": copy_gbs,
+        "frac_of_copy_same_size": bwd_gbs / copy_gbs,
     }
 
     # End to end through the public API, host buffers in and out.
