@@ -201,14 +201,17 @@ int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t sy
   if (pl->tma) {
     pl->k = bwd_tma_for(x_dtype, static_cast<int>(W), seq, silu);
     pl->max_smem = pl->k.smem;
-    // The partial count must not depend on seq_idx (the workspace query does not see it): size the
-    // grid by the lower occupancy of the two variants.
-    const KernelInfo k0 = bwd_tma_for(x_dtype, static_cast<int>(W), false, silu);
-    const KernelInfo k1 = bwd_tma_for(x_dtype, static_cast<int>(W), true, silu);
-    int o0 = 0, o1 = 0;
-    CC1D_TRY(occupancy(k0, k0.smem, dev, &o0));
-    CC1D_TRY(occupancy(k1, k1.smem, dev, &o1));
-    occ = std::min(o0, o1);
+    // The partial count must not depend on seq_idx or the activation (the workspace query sees
+    // neither): size the grid by the lowest occupancy of the four variants, all of which cover the
+    // same channels per CTA.
+    occ = 1 << 30;
+    for (int v = 0; v < 4; ++v) {
+      const KernelInfo kv = bwd_tma_for(x_dtype, static_cast<int>(W), (v & 1) != 0, (v & 2) != 0);
+      if (kv.d_tile != pl->k.d_tile) return CC1D_ERR_INVALID;
+      int o = 0;
+      CC1D_TRY(occupancy(kv, kv.smem, dev, &o));
+      occ = std::min(occ, o);
+    }
   } else {
     pl->k = bwd_generic_for(x_dtype, static_cast<int>(W));
     pl->max_smem = generic_bwd_smem(kGenericMaxWidth);
@@ -389,7 +392,7 @@ int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
   if (pl.tma) {
     BwdWalkParams p{};
     const int PADi = static_cast<int>(PAD);
-    const int box_d = pl.k.d_tile / 4;  // one channel block per consumer warp
+    const int box_d = pl.k.box_d;  // one channel block per consumer warp
     if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, box_d, pl.k.t_tile + PADi) &&
         encode_3d(&p.tmap_dy, dout, x_dtype, B, T, D, stride_dout_batch, stride_dout_time, box_d, pl.k.t_tile)) {
       int occ = 0;

@@ -4,8 +4,9 @@
 //   dx[t]  = sum_{j=0..W-1} w[W-1-j] dz[t+j]                                  (+ dfinal_states)
 //   dw[k] += dz[t] x[t-(W-1)+k],  db += dz[t]                                 (over all b, t)
 //
-// Work decomposition. A CTA owns a channel group of 4 x D_TILE channels (one 128-channel block of
-// bf16/fp16, or 64 of fp32, per consumer warp) and one contiguous stretch of L rows of the
+// Work decomposition. A CTA owns a channel group of WARPS x D_TILE channels (one channel block per
+// consumer warp: 128 channels of bf16/fp16 with SiLU, 64 without, 64 of fp32) and one contiguous
+// stretch of L rows of the
 // flattened (batch, time) index, i.e. one or two contiguous time segments of batch rows. It walks
 // each segment backwards in time, 16 rows per pipeline stage, from W-1 rows past the segment's end
 // (the halo whose dz the segment's last dx rows need) down to the segment's first row, and then,
@@ -13,11 +14,11 @@
 // the walk is continuous, every row's dz is computed once; only the W-1 halo rows per segment are
 // computed twice. The dz of the W-1 most recent rows, and all partial sums, stay in registers.
 //
-// Each CTA runs one producer warp, which issues per stage 4 TMA loads of x (rows a_lo-(W-1) ..
-// a_lo+15) and 4 of dout (rows a_lo .. a_lo+15) into a 2-stage mbarrier ring and writes the stage's
-// seq_idx window, and 4 consumer warps. Stages are aligned to the bottom of each segment, so the
+// Each CTA runs one producer warp, which issues per stage one TMA load of x (rows a_lo-(W-1) ..
+// a_lo+15) and one of dout (rows a_lo .. a_lo+15) per channel block into a 2-stage mbarrier ring
+// and writes the stage's seq_idx window, and the consumer warps. Stages are aligned to the bottom of each segment, so the
 // last stage of a segment starts exactly at its first row; only the segment's top stage can be
-// partial. Consumer lanes own CPT consecutive channels (an 8-byte vector) and compute in fp32 pairs
+// partial. Consumer lanes own CPT consecutive channels (a 4- or 8-byte vector) and compute in fp32 pairs
 // with the sm_100 f32x2 instructions. A stage whose 16 rows all belong to the segment (no halo, no
 // initial-state rows, no final-state rows, channels in range) runs a copy of the step loop without
 // any per-row checks.
@@ -34,14 +35,19 @@
 
 namespace cc1d {
 
-template <typename T, int W>
+// Per-lane vector width and consumer warps per CTA. With SiLU the kernel is bound by arithmetic
+// latency and runs best with 8-byte lanes (4 channels of bf16) and 4 warps per CTA; without it the
+// kernel is bandwidth-bound and 4-byte lanes with 8 warps per CTA keep more rows in flight (both
+// measured on B200 at BASELINE config 2).
+template <typename T, int W, bool SILU>
 struct BwdCfg {
   static constexpr int ES = static_cast<int>(sizeof(T));
-  static constexpr int ROW_BYTES = 256;          // one channel block's row segment
+  static constexpr int VEC = (SILU || W > 4 || ES == 4) ? 8 : 4;  // bytes per lane
+  static constexpr int ROW_BYTES = 32 * VEC;     // one channel block's row segment
   static constexpr int D_TILE = ROW_BYTES / ES;  // channels per warp
-  static constexpr int CPT = 8 / ES;             // channels per lane
+  static constexpr int CPT = VEC / ES;           // channels per lane
   static constexpr int NP = CPT / 2;             // fp32 pairs per lane
-  static constexpr int WARPS = 4;                // consumer warps = channel blocks per CTA
+  static constexpr int WARPS = VEC == 8 ? 4 : 8; // consumer warps = channel blocks per CTA
   static constexpr int THREADS = WARPS * 32 + 32;
   static constexpr int DG = WARPS * D_TILE;      // channels per CTA
   static constexpr int RS = 16;                  // rows per stage
@@ -101,9 +107,9 @@ struct SegmentWalk {
 };
 
 template <typename T, int W, bool SEQ, bool SILU>
-__global__ void __launch_bounds__(BwdCfg<T, W>::THREADS, BwdCfg<T, W>::MIN_CTAS)
+__global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU>::MIN_CTAS)
     cc1d_bwd_walk_kernel(const __grid_constant__ BwdWalkParams p) {
-  using C = BwdCfg<T, W>;
+  using C = BwdCfg<T, W, SILU>;
   constexpr int PAD = C::PAD, RS = C::RS, CPT = C::CPT, NP = C::NP, S = C::STAGES;
   constexpr int DT = C::D_TILE;
   constexpr bool FAST = sizeof(T) == 2;

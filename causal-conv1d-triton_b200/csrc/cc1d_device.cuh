@@ -186,14 +186,16 @@ __device__ __forceinline__ uint32_t f2_to_word(float2 f) {
 template <typename T, int CPT>
 __device__ __forceinline__ void load_vec(const T* p, float2 (&v)[CPT / 2]) {
   constexpr int NW = CPT * static_cast<int>(sizeof(T)) / 4;
-  static_assert(NW == 2 || NW == 4, "8- or 16-byte vectors");
+  static_assert(NW == 1 || NW == 2 || NW == 4, "4-, 8- or 16-byte vectors");
   uint32_t w[NW];
   if constexpr (NW == 4) {
     const uint4 q = *reinterpret_cast<const uint4*>(p);
     w[0] = q.x, w[1] = q.y, w[2] = q.z, w[3] = q.w;
-  } else {
+  } else if constexpr (NW == 2) {
     const uint2 q = *reinterpret_cast<const uint2*>(p);
     w[0] = q.x, w[1] = q.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
   }
   if constexpr (sizeof(T) == 4) {
 #pragma unroll
@@ -218,8 +220,10 @@ __device__ __forceinline__ void store_vec(T* p, const float2 (&v)[CPT / 2]) {
   }
   if constexpr (NW == 4)
     *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
-  else
+  else if constexpr (NW == 2)
     *reinterpret_cast<uint2*>(p) = make_uint2(w[0], w[1]);
+  else
+    *reinterpret_cast<uint32_t*>(p) = w[0];
 }
 
 // Scalar load of element `i` of a buffer whose element type is given at run time.

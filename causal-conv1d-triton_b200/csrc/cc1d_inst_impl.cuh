@@ -15,9 +15,9 @@ KernelInfo fwd_tma_one() {
 }
 template <typename T, int W, bool SEQ, bool SILU>
 KernelInfo bwd_tma_one() {
-  using C = BwdCfg<T, W>;
+  using C = BwdCfg<T, W, SILU>;
   return {reinterpret_cast<const void*>(&cc1d_bwd_walk_kernel<T, W, SEQ, SILU>), C::SMEM_BYTES, C::THREADS, C::DG,
-          C::RS};
+          C::RS, C::D_TILE};
 }
 template <typename T, int W>
 KernelInfo fwd_tma_w(bool seq, bool silu) {
