@@ -4,6 +4,6 @@ Drop-in for jxiong21029/causal-conv1d-triton (`from causal_conv1d_triton import 
 causal_conv1d_triton/__init__.py:1-3): `from causal_conv1d_b200 import causal_conv1d_fn`.
 """
 
-from .causal_conv1d import causal_conv1d_fn
+from .causal_conv1d import causal_conv1d_fn, causal_conv1d_update, seq_idx_from_cu_seqlens
 
-__all__ = ["causal_conv1d_fn"]
+__all__ = ["causal_conv1d_fn", "causal_conv1d_update", "seq_idx_from_cu_seqlens"]

@@ -30,6 +30,9 @@ SIGNATURES = {
     "cc1d_abi_version": ([], _I),
     "cc1d_fwd": ([_P, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
                   _I, _I, _I, _I, _I, _P], _I),
+    "cc1d_seq_idx_from_cu_seqlens": ([_P, _I64, _P, _I64, _I64, _P], _I),
+    "cc1d_update": ([_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                     _I, _I, _I, _I, _I, _P], _I),
     "cc1d_bwd_workspace_bytes": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I],
                                  _I64),
     "cc1d_bwd": ([_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P,

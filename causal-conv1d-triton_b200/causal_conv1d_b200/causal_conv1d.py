@@ -244,3 +244,86 @@ def causal_conv1d_fn(
         out, final_states = result
         result = out, final_states_out.copy_(final_states)
     return result
+
+
+def causal_conv1d_update(
+    x: Tensor,
+    conv_state: Tensor,
+    weight: Tensor,
+    bias: Tensor | None = None,
+    activation: str | None = None,
+    conv_state_indices: Tensor | None = None,
+) -> Tensor:
+    """Decode step: run the new rows `x` through the conv, continuing from `conv_state`.
+
+    x: (batch, dim) for one new row per batch entry, or (batch, seqlen, dim) for several;
+        contiguous along dim
+    conv_state: (n_slots, width - 1, dim), the inputs preceding x (the reference's state layout,
+        causal_conv1d.py:597-599); updated in place to the last width - 1 rows of
+        concat(conv_state, x), i.e. the final_states the forward would return
+    weight: (dim, width); bias: (dim,); activation: None, "silu" or "swish"
+    conv_state_indices: optional (batch,) integer slot of each batch entry in conv_state; a
+        negative slot leaves that entry's output unwritten and its state untouched
+
+    Returns the output rows, shaped like x, in x's dtype: the same values causal_conv1d_fn gives for
+    these rows with initial_states=conv_state. The reference has no decode kernel; this is its
+    single-step companion. Not differentiable (inference only).
+    """
+    if activation not in (None, "silu", "swish"):
+        raise NotImplementedError("activation must be None, silu, or swish")
+    squeeze = x.ndim == 2
+    if squeeze:
+        x = x.unsqueeze(1)
+    assert x.ndim == 3, "x must be (batch, dim) or (batch, seqlen, dim)"
+    B, L, D = x.shape
+    assert weight.ndim == 2 and weight.shape[0] == D, "weight must be (dim, width)"
+    W = weight.shape[1]
+    assert W >= 2, "width must be >= 2"
+    assert x.is_cuda and weight.device == x.device and conv_state.device == x.device
+    assert conv_state.ndim == 3 and conv_state.shape[1:] == (W - 1, D)
+    assert conv_state.is_contiguous(), "conv_state must be contiguous (it is updated in place)"
+    assert bias is None or bias.shape == (D,)
+    if conv_state_indices is None:
+        assert conv_state.shape[0] >= B
+    else:
+        assert conv_state_indices.shape == (B,)
+        conv_state_indices = conv_state_indices.to(device=x.device, dtype=torch.int32).contiguous()
+    if x.dtype not in _FLOAT or conv_state.dtype not in _FLOAT:
+        raise TypeError("x and conv_state must be float32, float16 or bfloat16")
+    x = _channels_contiguous(x)
+    w, b = _as_float(weight.contiguous()), _as_float(bias.contiguous() if bias is not None else None)
+    out = torch.empty(B, L, D, device=x.device, dtype=x.dtype)
+    with _DeviceGuard(x.device):
+        check(
+            lib.cc1d_update(
+                x.data_ptr(), x.stride(0), x.stride(1), conv_state.data_ptr(),
+                _ptr(conv_state_indices), w.data_ptr(), _ptr(b), out.data_ptr(), B, L, D, W,
+                DTYPE_CODE[x.dtype], DTYPE_CODE[conv_state.dtype], DTYPE_CODE[w.dtype], _code(b),
+                int(activation is not None), _stream(x.device),
+            ),
+            "causal_conv1d update",
+        )
+    return out.squeeze(1) if squeeze else out
+
+
+def seq_idx_from_cu_seqlens(cu_seqlens: Tensor, seqlen: int) -> Tensor:
+    """seq_idx (int32) for packed variable-length sequences, built on the device.
+
+    cu_seqlens: (n_seqs + 1,) for a single packed row, or (batch, n_seqs + 1) for one set of
+        boundaries per row; non-decreasing from 0. Row b's sequences are [cu[i], cu[i+1]).
+    seqlen: length T of each packed row.
+
+    Returns (batch, seqlen) int32 (batch = 1 for 1-D cu_seqlens): each position's sequence id, and
+    -1 (padding: zero output in causal_conv1d_fn) at or past the last boundary.
+    """
+    cu = cu_seqlens.unsqueeze(0) if cu_seqlens.ndim == 1 else cu_seqlens
+    assert cu.ndim == 2 and cu.shape[1] >= 2, "cu_seqlens must be (n_seqs + 1,) or (batch, n_seqs + 1)"
+    assert cu.is_cuda, "cu_seqlens must be on a CUDA device"
+    cu = cu.to(torch.int32).contiguous()
+    B, n1 = cu.shape
+    seq_idx = torch.empty(B, seqlen, device=cu.device, dtype=torch.int32)
+    with _DeviceGuard(cu.device):
+        check(lib.cc1d_seq_idx_from_cu_seqlens(cu.data_ptr(), n1 - 1, seq_idx.data_ptr(), B, seqlen,
+                                               _stream(cu.device)),
+              "seq_idx_from_cu_seqlens")
+    return seq_idx

@@ -12,6 +12,8 @@
 #include "causal_conv1d_b200.h"
 #include "cc1d_dispatch.h"
 #include "cc1d_reduce_kernels.cuh"
+#include "cc1d_seqidx_kernel.cuh"
+#include "cc1d_update_kernel.cuh"
 
 namespace cc1d {
 
@@ -335,6 +337,46 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
   if (grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
   void* args[] = {&g};
   CC1D_TRY_CUDA(cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(grid)), dim3(k.threads), args, k.smem, stream));
+  return CC1D_OK;
+}
+
+int cc1d_seq_idx_from_cu_seqlens(const int32_t* cu_seqlens, int64_t n_seqs, int32_t* seq_idx, int64_t batch,
+                                 int64_t seqlen, void* stream_) {
+  if (n_seqs < 1 || batch < 0 || seqlen < 0 || batch >= (int64_t(1) << 31) || seqlen >= (int64_t(1) << 31) ||
+      n_seqs >= (int64_t(1) << 31))
+    return CC1D_ERR_INVALID;
+  if (batch == 0 || seqlen == 0) return CC1D_OK;
+  if (!cu_seqlens || !seq_idx) return CC1D_ERR_INVALID;
+  const int64_t n = batch * seqlen;
+  if (cdiv(n, 256) >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+  cc1d_seq_idx_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0, static_cast<cudaStream_t>(stream_)>>>(
+      cu_seqlens, static_cast<int>(n_seqs), seq_idx, static_cast<int>(batch), static_cast<int>(seqlen));
+  CC1D_TRY_CUDA(cudaGetLastError());
+  return CC1D_OK;
+}
+
+int cc1d_update(const void* x, int64_t stride_x_batch, int64_t stride_x_time, void* conv_state,
+                const int32_t* state_indices, const void* weight, const void* bias, void* out, int64_t batch,
+                int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int state_dtype, int weight_dtype,
+                int bias_dtype, int silu, void* stream_) {
+  if (!valid_dtype(x_dtype) || !valid_dtype(state_dtype) || !valid_dtype(weight_dtype) ||
+      (bias && !valid_dtype(bias_dtype)))
+    return CC1D_ERR_INVALID;
+  CC1D_TRY(check_sizes(batch, seqlen, dim, width));
+  if (batch == 0 || dim == 0 || seqlen == 0) return CC1D_OK;
+  if (!x || !conv_state || !weight || !out) return CC1D_ERR_INVALID;
+  DeviceInfo di;
+  int dev = 0;
+  CC1D_TRY(device_info(&di, &dev));
+  UpdateParams u{};
+  u.x = x, u.state = conv_state, u.indices = state_indices, u.weight = weight, u.bias = bias, u.out = out;
+  u.sxb = stride_x_batch, u.sxt = stride_x_time;
+  u.B = static_cast<int>(batch), u.L = static_cast<int>(seqlen), u.D = static_cast<int>(dim), u.W = static_cast<int>(width);
+  u.x_dtype = x_dtype, u.s_dtype = state_dtype, u.w_dtype = weight_dtype, u.b_dtype = bias_dtype, u.silu = silu != 0;
+  const int64_t n = batch * dim;
+  if (cdiv(n, 256) >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+  cc1d_update_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0, static_cast<cudaStream_t>(stream_)>>>(u);
+  CC1D_TRY_CUDA(cudaGetLastError());
   return CC1D_OK;
 }
 

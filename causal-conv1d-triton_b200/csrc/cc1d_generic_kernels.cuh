@@ -42,6 +42,11 @@ __device__ __forceinline__ float sigmoid_generic(float z, bool fast) {
   return __fdividef(1.0f, 1.0f + __expf(-z));
 }
 
+// SiLU with the same per-element operations as the TMA forward's silu2.
+__device__ __forceinline__ float silu_generic(float z, bool fast) {
+  return fast ? silu2<true>(make_float2(z, z)).x : silu2<false>(make_float2(z, z)).x;
+}
+
 // Row t of concat(initial_states, x) at channel d in fp32 (causal_conv1d.py:28-41).
 template <typename T>
 __device__ __forceinline__ float x_at(const GenericParams& p, int b, int t, int d) {
@@ -94,7 +99,7 @@ __global__ void __launch_bounds__(GTHREADS) cc1d_fwd_generic_kernel(const Generi
       if (!p.seq || sq[r + k] == seq_t) z = fmaf(ws[k * GC + c], xs[(r + k) * GC + c], z);
     z += bias;
     if (p.seq && seq_t < 0) z = 0.0f;
-    if (p.silu) z = z * sigmoid_generic(z, FAST);
+    if (p.silu) z = silu_generic(z, FAST);
     if (d < p.D) static_cast<T*>(p.out)[(static_cast<int64_t>(b) * p.T + t0 + r) * p.D + d] = from_f<T>(z);
   }
 

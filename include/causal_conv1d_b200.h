@@ -66,6 +66,35 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
              void* stream);
 
 /*
+ * seq_idx for a packed variable-length batch, from cumulative sequence boundaries. The reference
+ * takes seq_idx directly (causal_conv1d.py:594-596) and leaves building it to the caller; this
+ * builds it on the device:
+ *   cu_seqlens   (B, n_seqs + 1) int32, row b non-decreasing from 0: its sequences are
+ *                [cu[b][i], cu[b][i+1])
+ *   seq_idx      (B, T) int32 out: the sequence id (0 .. n_seqs-1) of each position, -1 (padding)
+ *                at or past cu[b][n_seqs]
+ */
+int cc1d_seq_idx_from_cu_seqlens(const int32_t* cu_seqlens, int64_t n_seqs, int32_t* seq_idx,
+                                 int64_t batch, int64_t seqlen, void* stream);
+
+/*
+ * Decode-time update of the streaming state. No counterpart kernel in the reference, which only
+ * documents the state (`initial_states`/`final_states`, causal_conv1d.py:597-599); this applies L
+ * new rows per batch row without a full forward:
+ *   x               (B, L, D) at strides (stride_x_batch, stride_x_time, 1), type x_dtype
+ *   conv_state      (n_slots, W-1, D) contiguous, type state_dtype, updated in place to the last
+ *                   W-1 rows of concat(conv_state, x) (the final_states of the same forward)
+ *   state_indices   (B) int32 slot of each batch row in conv_state, or NULL for slot b; a negative
+ *                   slot skips the row (its output is left unwritten)
+ *   out             (B, L, D) contiguous, type x_dtype: the forward's output for these rows,
+ *                   computed with the same operations as cc1d_fwd
+ */
+int cc1d_update(const void* x, int64_t stride_x_batch, int64_t stride_x_time, void* conv_state,
+                const int32_t* state_indices, const void* weight, const void* bias, void* out,
+                int64_t batch, int64_t seqlen, int64_t dim, int64_t width, int x_dtype,
+                int state_dtype, int weight_dtype, int bias_dtype, int silu, void* stream);
+
+/*
  * Size in bytes of the fp32 workspace cc1d_bwd needs for its per-CTA weight/bias partial sums
  * (the `partials` buffer that `_bwd` allocates, causal_conv1d.py:493). Depends on the sizes, the
  * element type, the strides and 16-byte alignment of x and dout, and the current device.
