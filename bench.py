@@ -2,6 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton]
     torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+    python bench.py --sweep     (every BASELINE config, ours vs the reference's Triton kernels)
 
 Workload (the sweep the headline metric is quoted on, at its largest
 sequence length): per GPU x bf16 (B=8, T=32768, D=1024) ~ N(0,1), weight fp32 (1024, 4) ~ N(0, 1/4),
@@ -67,6 +68,9 @@ def parse():
     ap.add_argument("--no-bias-silu", action="store_true", help="the no-bias/no-activation mode")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time every BASELINE config through both implementations' public APIs "
+                         "(ours and the reference's Triton kernels) and print one JSON line each")
     return ap.parse_args()
 
 
@@ -255,8 +259,157 @@ def run_triton_reference(args, dev):
     return ref._fwd, ref._bwd
 
 
+# ---------------------------------------------------------------------------------------------
+# --sweep: every BASELINE.json config through the public API of both implementations.
+# ---------------------------------------------------------------------------------------------
+def _sweep_cases():
+    """(name, builder) for each BASELINE config; a builder returns the call's tensors on the host."""
+    def dense(B, T, D, W, wstd, bstd, silu, seed=0):
+        def build():
+            g = torch.Generator().manual_seed(seed)
+            x = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+            w = torch.randn(D, W, generator=g) * wstd
+            b = torch.randn(D, generator=g) * bstd if bstd else None
+            dy = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+            return dict(x=x, w=w, b=b, dy=dy, silu=silu)
+        return build
+
+    def varlen():
+        g = torch.Generator().manual_seed(4)
+        B, T, D, W = 4, 16384, 4352, 4
+        x = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+        w = torch.randn(D, W, generator=g) * 0.5
+        b = torch.randn(D, generator=g) * 0.1 ** 0.5
+        seq = torch.empty(B, T, dtype=torch.int32)
+        for r in range(B):
+            pad = int(torch.randint(0, 256, (1,), generator=g))
+            t, sid = 0, 0
+            while t < T - pad:
+                n = int(torch.randint(64, 4097, (1,), generator=g))
+                seq[r, t:min(t + n, T - pad)] = sid
+                t, sid = t + n, sid + 1
+            seq[r, T - pad:] = -1
+        init = torch.randn(B, W - 1, D, generator=g).to(torch.bfloat16)
+        dy = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+        return dict(x=x, w=w, b=b, dy=dy, silu=True, seq=seq, init=init)
+
+    def chain():
+        d = dense(16, 8192, 2048, 4, 0.5, 0.1 ** 0.5, True, seed=3)()
+        g = torch.Generator().manual_seed(33)
+        d["init"] = torch.randn(16, 3, 2048, generator=g).to(torch.bfloat16)
+        # Each chunk is its own leaf (a streaming caller gets the chunks one at a time); slicing one
+        # leaf would time torch's slice-backward (a full-size zero tensor per chunk), not the conv.
+        L = 8192 // 4
+        d["xs"] = [d["x"][:, i * L:(i + 1) * L].contiguous() for i in range(4)]
+        d["dys"] = [d["dy"][:, i * L:(i + 1) * L].contiguous() for i in range(4)]
+        return d
+
+    cases = [("cfg1 B=2 T=1024 D=512 W=4 bias+silu", dense(2, 1024, 512, 4, 1.0, 1.0, True))]
+    for T in (512, 2048, 8192, 32768):
+        cases.append((f"cfg2 B=8 T={T} D=1024 W=4 none", dense(8, T, 1024, 4, 0.5, 0, False)))
+        cases.append((f"cfg2 B=8 T={T} D=1024 W=4 bias+silu", dense(8, T, 1024, 4, 0.5, 0.1 ** 0.5, True)))
+    cases.append(("cfg3 B=16 T=8192 D=2048 W=4 bias+silu, 4 chained chunks", chain))
+    cases.append(("cfg4 B=4 T=16384 D=4352 W=4 varlen seq_idx+init bias+silu", varlen))
+    cases.append(("cfg5 B=64 T=8192 D=8192 W=8 bias+silu, 1 GPU", dense(64, 8192, 8192, 8, 8 ** -0.5, 0.1 ** 0.5, True)))
+    return cases
+
+
+def _sweep_step(fn, t, grad):
+    """One call of the workload through `fn` (a causal_conv1d_fn): forward, and backward if grad."""
+    act = "silu" if t["silu"] else None
+    if "xs" in t:
+        state, outs = t["init"], []
+        for xc in t["xs"]:
+            o, state = fn(xc, t["w"], t["b"], initial_states=state, return_final_states=True,
+                          activation=act)
+            outs.append(o)
+        if grad:
+            torch.autograd.backward(outs, t["dys"])
+        return outs
+    out = fn(t["x"], t["w"], t["b"], seq_idx=t.get("seq"), initial_states=t.get("init"), activation=act)
+    if grad:
+        out.backward(t["dy"])
+    return out
+
+
+def run_sweep(args):
+    import statistics as st
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from causal_conv1d_b200 import causal_conv1d_fn as ours
+
+    sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+    try:
+        from causal_conv1d_triton import causal_conv1d_fn as ref
+    except Exception as e:  # the reference install is optional for the sweep
+        ref, ref_err = None, str(e)
+    peak, _ = measured_peak()
+    for name, build in _sweep_cases():
+        h = build()
+        t = {k: (v.to(dev) if torch.is_tensor(v) else [u.to(dev) for u in v] if isinstance(v, list) else v)
+             for k, v in h.items()}
+        for k in ("x", "w", "b", "init"):
+            if t.get(k) is not None:
+                t[k].requires_grad_(True)
+        for xc in t.get("xs", []):
+            xc.requires_grad_(True)
+        B, T, D = h["x"].shape
+        W = h["w"].shape[1]
+        fb, bb = algo_bytes(B, T, D, W)
+        impls = [("ours", ours)] + ([("reference-triton", ref)] if ref is not None else [])
+        res = {n: {"fwd": [], "fwdbwd": []} for n, _ in impls}
+        outs = {}
+        for n, fn in impls:  # warm-up and results for the agreement check
+            with torch.no_grad():
+                outs[n] = _sweep_step(fn, t, False)
+            _sweep_step(fn, t, True)
+        torch.cuda.synchronize()
+        reps = max(2, min(50, int(4e9 / (fb + bb))))
+        for _ in range(5):
+            for n, fn in impls:
+                e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                e[0].record()
+                with torch.no_grad():
+                    for _ in range(reps):
+                        _sweep_step(fn, t, False)
+                e[1].record()
+                for _ in range(reps):
+                    for v in [t.get(k) for k in ("x", "w", "b", "init")] + t.get("xs", []):
+                        if v is not None:
+                            v.grad = None
+                    _sweep_step(fn, t, True)
+                e[2].record()
+                torch.cuda.synchronize()
+                res[n]["fwd"].append(e[0].elapsed_time(e[1]) / reps * 1e3)
+                res[n]["fwdbwd"].append(e[1].elapsed_time(e[2]) / reps * 1e3)
+        agree = None
+        if ref is not None:
+            a = torch.cat([o.flatten() for o in (outs["ours"] if isinstance(outs["ours"], list) else [outs["ours"]])]).float()
+            r = torch.cat([o.flatten() for o in (outs["reference-triton"] if isinstance(outs["reference-triton"], list) else [outs["reference-triton"]])]).float()
+            agree = bool(((a - r).abs() <= 1e-2 + 1e-2 * r.abs()).all().item())
+        line = {"sweep": name, "reps": reps, "outputs_agree_within_bf16_tol": agree}
+        for n in res:
+            f, fbw = st.median(res[n]["fwd"]), st.median(res[n]["fwdbwd"])
+            line[n] = {"fwd_us": f, "fwd_bwd_us": fbw, "fwd_gbs": fb / f / 1e3,
+                       "fwd_bwd_gbs": (fb + bb) / fbw / 1e3,
+                       "fwd_frac_of_measured": fb / f / 1e3 / peak,
+                       "fwd_bwd_frac_of_measured": (fb + bb) / fbw / 1e3 / peak}
+        if ref is not None:
+            line["speedup_fwd"] = line["reference-triton"]["fwd_us"] / line["ours"]["fwd_us"]
+            line["speedup_fwd_bwd"] = line["reference-triton"]["fwd_bwd_us"] / line["ours"]["fwd_bwd_us"]
+        else:
+            line["reference-triton"] = {"unavailable": ref_err}
+        print(json.dumps(line), flush=True)
+        del t, h, outs
+        torch.cuda.empty_cache()
+
+
 def main():
     args = parse()
+    if args.sweep:
+        run_sweep(args)
+        return
     if args.impl == "reference":
         run_reference_cpu(args)
         return

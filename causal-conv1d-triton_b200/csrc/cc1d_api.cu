@@ -313,7 +313,7 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
       p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
       const int64_t M = B * p.n_tt;
       const int64_t cap = static_cast<int64_t>(di.sms) * occ;
-      const int64_t P = std::max<int64_t>(1, std::min<int64_t>(M, cap / p.n_db));
+      const int64_t P = k.persistent ? std::max<int64_t>(1, std::min<int64_t>(M, cap / p.n_db)) : M;
       const int64_t grid = P * p.n_db;
       if (grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
       void* args[] = {&p};
