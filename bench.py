@@ -527,7 +527,7 @@ def main():
     line["impl"] = "ours"
     line["gpu_launches"] = 3 * args.steps
     line["roofline"] = {
-        "bound": "hbm", "kernel": "cc1d_bwd_tma_kernel (+ reduce)", "achieved": bwd_gbs,
+        "bound": "hbm", "kernel": "cc1d_bwd_walk_kernel (+ reduce)", "achieved": bwd_gbs,
         "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak, "peak_source": f"{peak_kind} hbm_gbs",
         "traffic": BWD_DRAM_BYTES_PER_LAUNCH * (B * T) / BWD_DRAM_ROWS,
         "algorithmic_bytes": bbytes,

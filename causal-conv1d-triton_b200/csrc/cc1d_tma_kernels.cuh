@@ -2,19 +2,23 @@
 //
 //   out[b,t,d] = act(bias[d] + sum_k weight[d,k] * x[b, t-(W-1)+k, d])
 //
-// Work decomposition. The (B, T, D) input is cut into tiles of T_TILE = 64 time rows (16 per warp)
-// by D_TILE channels (one 256-byte row segment: 128 channels of bf16/fp16, 64 of fp32), one tile per CTA,
+// Work decomposition. The (B, T, D) input is cut into tiles of T_TILE = 64 time rows by D_TILE
+// channels (one 256-byte row segment: 128 channels of bf16/fp16, 64 of fp32), one tile per CTA,
 // the grid covering every tile with the channel block fastest, so that the CTAs resident at any
 // moment sweep the tensor front to back together (each tile's W-1 halo rows were fetched by the
 // neighbouring tile moments earlier and come from L2).
 //
 // A CTA's thread 0 issues one 3-D TMA bulk tensor load of the tile and its halo into shared memory
-// (rows outside [0, T) zero-filled by the TMA unit), completion counted on an mbarrier; the warps
-// load the taps and the tile's seq_idx window meanwhile. Warp rg owns the R = 16 consecutive rows
-// [t0 + 16 rg, t0 + 16 rg + 16); its lane owns CPT consecutive channels (one 8-byte vector: 4
-// channels of bf16/fp16, 2 of fp32). Each thread reads its rows from shared memory, computes in fp32
-// pairs with the sm_100 f32x2 instructions and stores 8-byte vectors straight to global memory (a
-// warp writes one contiguous 256-byte row segment per store).
+// (rows outside [0, T) zero-filled by the TMA unit), completion counted on an mbarrier; the
+// threads load the taps and the tile's seq_idx window meanwhile. The 128 threads form RG row
+// groups of LANES_D threads; row group rg owns the R = 64 / RG consecutive rows [t0 + R rg,
+// t0 + R rg + R), and each of its threads owns CPT consecutive channels of one vector. Up to W = 4
+// (and for fp32) a vector is 8 bytes: 4 channels of bf16/fp16 (2 of fp32), a warp per row, R = 16.
+// Wider 16-bit windows use 4-byte vectors (2 channels, two warps per row, R = 32): with 4 channels a
+// thread's W x 4 fp32 taps and (W-1) x 4 window values alone fill the 80 registers that 6 CTAs per
+// SM allow, and occupancy, not arithmetic, sets this kernel's speed. Each thread reads its rows
+// from shared memory, computes in fp32 pairs with the sm_100 f32x2 instructions and stores its
+// vector straight to global memory (a warp writes a contiguous 256- or 128-byte row segment).
 //
 // The backward is in cc1d_bwd_kernel.cuh; TileCfg's constants, the tap loaders and the seq_idx
 // convention here are shared with it.
@@ -33,16 +37,16 @@ struct TileCfg {
   static constexpr int ES = static_cast<int>(sizeof(T));
   static constexpr int ROW_BYTES = 256;               // bytes of one tile row (TMA box inner extent)
   static constexpr int D_TILE = ROW_BYTES / ES;       // channels per tile
-  static constexpr int VEC_BYTES = 8;                 // one 8-byte vector per thread per row
-  static constexpr int CPT = VEC_BYTES / ES;          // channels per thread (4, or 2 for fp32)
+  static constexpr int VEC_BYTES = (ES == 2 && W > 4) ? 4 : 8;  // one vector per thread per row
+  static constexpr int CPT = VEC_BYTES / ES;          // channels per thread (4 or 2)
   static constexpr int NP = CPT / 2;                  // fp32 pairs per thread
-  static constexpr int LANES_D = D_TILE / CPT;        // threads across one tile row: a whole warp
+  static constexpr int LANES_D = D_TILE / CPT;        // threads across one tile row: 32 or 64
   static constexpr int CONSUMERS = 128;               // threads per CTA
-  static constexpr int RG = CONSUMERS / LANES_D;      // row groups per tile: one per warp
-  static constexpr int T_TILE = 16 * RG;
-  static constexpr int R = T_TILE / RG;               // rows per thread per tile
+  static constexpr int RG = CONSUMERS / LANES_D;      // row groups per tile
+  static constexpr int T_TILE = 64;
+  static constexpr int R = T_TILE / RG;               // rows per thread per tile: 16 or 32
   static constexpr int PAD = W - 1;
-  static_assert(LANES_D == 32, "a warp spans one tile row");
+  static_assert(LANES_D % 32 == 0 && RG * LANES_D == CONSUMERS, "row groups are whole warps");
   static_assert(W >= 2 && W <= 8, "TMA path covers widths 2..8");
   static_assert(R >= PAD, "only row group 0 of the first tile reads rows t < 0");
 };
@@ -56,8 +60,9 @@ struct FwdLayout {
   static constexpr int XROWS = C::T_TILE + C::PAD;    // rows [t0 - PAD, t0 + T_TILE)
   static constexpr int XBYTES = XROWS * C::ROW_BYTES;
   static constexpr int SEQ_BYTES = SEQ ? (XROWS * 4 + 127) / 128 * 128 : 0;
-  // Registers are bounded for 6 CTAs (24 warps) per SM; 17-18 KB of shared memory each.
-  static constexpr int MIN_CTAS = 6;
+  // Registers are bounded for 6 CTAs (24 warps) per SM with 8-byte vectors, 8 CTAs with 4-byte
+  // vectors; 17-18 KB of shared memory each.
+  static constexpr int MIN_CTAS = C::VEC_BYTES == 4 ? 8 : 6;
   static constexpr int SMEM_BYTES = kSmemAlign + kBarBytes + XBYTES + SEQ_BYTES;
 };
 
@@ -103,27 +108,34 @@ __device__ __forceinline__ void load_taps(const void* weight, int w_dtype, const
   }
 }
 
-// load_taps for fp32 weights and bias with 16-byte loads: a thread's CPT channels x W taps are
-// CPT * W consecutive floats of the (D, W) weight. Falls back to load_taps for other dtypes or
-// addresses that are not 16-byte aligned. Requires an even CPT.
+// load_taps for fp32 weights and bias with vector loads: a thread's CPT channels x W taps are
+// CPT * W consecutive floats of the (D, W) weight, read as float4s when their count and address
+// allow, else as float2s; the bias likewise. Falls back to load_taps for other dtypes or
+// misaligned addresses. Requires an even CPT.
 template <int W, int NP>
 __device__ __forceinline__ void load_taps_fast(const void* weight, int w_dtype, const void* bias, int b_dtype, int d,
                                                bool dvalid, float2 (&w)[W][NP], float2 (&bv)[NP]) {
   constexpr int CPT = 2 * NP;
+  constexpr int WV = (CPT * W) % 4 == 0 ? 4 : 2;  // floats per weight load
+  constexpr int BV = CPT % 4 == 0 ? 4 : 2;        // floats per bias load
   const float* wf = static_cast<const float*>(weight) + static_cast<int64_t>(d) * W;
-  const bool vec_w = w_dtype == kF32 && (CPT * W) % 4 == 0 && (reinterpret_cast<uintptr_t>(wf) & 15) == 0;
-  const bool vec_b = bias == nullptr ||
-                     (b_dtype == kF32 && CPT % 4 == 0 &&
-                      ((reinterpret_cast<uintptr_t>(static_cast<const float*>(bias) + d) & 15) == 0));
+  const float* bf = bias != nullptr ? static_cast<const float*>(bias) + d : nullptr;
+  const bool vec_w = w_dtype == kF32 && (reinterpret_cast<uintptr_t>(wf) & (4 * WV - 1)) == 0;
+  const bool vec_b = bias == nullptr || (b_dtype == kF32 && (reinterpret_cast<uintptr_t>(bf) & (4 * BV - 1)) == 0);
   if (!dvalid || !vec_w || !vec_b) {
     load_taps<W, NP>(weight, w_dtype, bias, b_dtype, d, dvalid, w, bv);
     return;
   }
   float wv[CPT * W];
 #pragma unroll
-  for (int q = 0; q < CPT * W / 4; ++q) {
-    const float4 v = __ldg(reinterpret_cast<const float4*>(wf) + q);
-    wv[4 * q] = v.x, wv[4 * q + 1] = v.y, wv[4 * q + 2] = v.z, wv[4 * q + 3] = v.w;
+  for (int q = 0; q < CPT * W / WV; ++q) {
+    if constexpr (WV == 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(wf) + q);
+      wv[4 * q] = v.x, wv[4 * q + 1] = v.y, wv[4 * q + 2] = v.z, wv[4 * q + 3] = v.w;
+    } else {
+      const float2 v = __ldg(reinterpret_cast<const float2*>(wf) + q);
+      wv[2 * q] = v.x, wv[2 * q + 1] = v.y;
+    }
   }
 #pragma unroll
   for (int i = 0; i < NP; ++i)
@@ -132,14 +144,16 @@ __device__ __forceinline__ void load_taps_fast(const void* weight, int w_dtype, 
   if (bias == nullptr) {
 #pragma unroll
     for (int i = 0; i < NP; ++i) bv[i] = make_float2(0.f, 0.f);
-  } else {
-    const float* bf = static_cast<const float*>(bias) + d;
+  } else if constexpr (BV == 4) {
 #pragma unroll
     for (int q = 0; q < CPT / 4; ++q) {
       const float4 v = __ldg(reinterpret_cast<const float4*>(bf) + q);
       bv[2 * q] = make_float2(v.x, v.y);
       bv[2 * q + 1] = make_float2(v.z, v.w);
     }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NP; ++i) bv[i] = __ldg(reinterpret_cast<const float2*>(bf) + i);
   }
 }
 
@@ -181,7 +195,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   const int tt = rest % p.n_tt;
   const int b = rest / p.n_tt;
   const int t0 = tt * C::T_TILE;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rg = threadIdx.x / C::LANES_D, lane = threadIdx.x % C::LANES_D;
 
   if (threadIdx.x == 0) {
     mbar_init(full, 1);
@@ -206,7 +220,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   if (!mbar_wait(full, 0, p.status)) return;
 
   const T* xt = reinterpret_cast<const T*>(tile) + lane * CPT;  // local row r <-> global row t0 - PAD + r
-  const int rb = warp * R;  // local row of global row ts - PAD
+  const int rb = rg * R;  // local row of global row ts - PAD
   const int ts = t0 + rb;
 
   // Before the step at row t: xw[k] = x[t - PAD + k], k < PAD.
@@ -263,7 +277,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   }
 
   // final_states = last PAD rows of concat(initial_states, x) (causal_conv1d.py:153-164).
-  if (p.final_states != nullptr && tt == p.n_tt - 1 && warp == 0 && dvalid) {
+  if (p.final_states != nullptr && tt == p.n_tt - 1 && rg == 0 && dvalid) {
 #pragma unroll
     for (int q = 0; q < PAD; ++q) {
       const int src = p.T - PAD + q;

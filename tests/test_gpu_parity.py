@@ -163,7 +163,7 @@ def check_vs_oracle(cc, B, T, D, W, dt, has_bias, silu, has_init, has_seq, ret_f
 
 
 SWEEP = []
-for dt, W in itertools.product([torch.bfloat16, torch.float16, torch.float32], [2, 3, 4, 5, 8]):
+for dt, W in itertools.product([torch.bfloat16, torch.float16, torch.float32], [2, 3, 4, 5, 6, 7, 8]):
     SWEEP.append((dt, W))
 
 
