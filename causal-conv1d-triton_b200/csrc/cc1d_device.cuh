@@ -22,6 +22,17 @@ enum : unsigned { kStatusWaitTimeout = 1u };
 // Every wait on an mbarrier gives up after this long, records kStatusWaitTimeout and returns.
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s
 
+// Calls f(std::integral_constant<int, I>{}) for I = B .. E-1 in order. Unlike `#pragma unroll`,
+// the body is always instantiated once per index, so arrays indexed by I stay in registers with
+// fixed assignments (a ring indexed by (I + k) % N moves no values).
+template <int B, int E, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+  if constexpr (B < E) {
+    f(std::integral_constant<int, B>{});
+    static_for<B + 1, E>(f);
+  }
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

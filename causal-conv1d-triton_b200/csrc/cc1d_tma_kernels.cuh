@@ -223,8 +223,10 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   const int rb = rg * R;  // local row of global row ts - PAD
   const int ts = t0 + rb;
 
-  // Before the step at row t: xw[k] = x[t - PAD + k], k < PAD.
-  float2 xw[PAD][NP];
+  // Ring of the last PAD + 1 input rows: local row j (global row ts - PAD + j) sits in slot
+  // j % NW. Every index below is a compile-time constant, so the ring never moves a value.
+  constexpr int NW = PAD + 1;
+  float2 xw[NW][NP];
   if (p.init != nullptr && ts == 0) {
 #pragma unroll
     for (int k = 0; k < PAD; ++k) {
@@ -241,20 +243,21 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   }
 
   T* orow = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.T + ts) * D + d;
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    float2 xr[NP];
-    load_vec<T, CPT>(xt + (rb + PAD + r) * DT, xr);
+  const bool full_rows = dvalid && ts + R <= p.T;
+  static_for<0, R>([&](auto rc) {
+    constexpr int r = decltype(rc)::value;
+    constexpr int cur = (r + PAD) % NW;
+    load_vec<T, CPT>(xt + (rb + PAD + r) * DT, xw[cur]);
     const int seq_t = SEQ ? sq[rb + PAD + r] : 0;
     // z = w[PAD] x[t], then taps k = 0..PAD-1 oldest first, then bias (causal_conv1d.py:129-136).
     float2 z[NP];
 #pragma unroll
-    for (int i2 = 0; i2 < NP; ++i2) z[i2] = fmul2(w[PAD][i2], xr[i2]);
+    for (int i2 = 0; i2 < NP; ++i2) z[i2] = fmul2(w[PAD][i2], xw[cur][i2]);
 #pragma unroll
     for (int k = 0; k < PAD; ++k) {
       if (!SEQ || sq[rb + r + k] == seq_t) {
 #pragma unroll
-        for (int i2 = 0; i2 < NP; ++i2) z[i2] = ffma2(w[k][i2], xw[k][i2], z[i2]);
+        for (int i2 = 0; i2 < NP; ++i2) z[i2] = ffma2(w[k][i2], xw[(r + k) % NW][i2], z[i2]);
       }
     }
 #pragma unroll
@@ -267,14 +270,8 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
 #pragma unroll
       for (int i2 = 0; i2 < NP; ++i2) z[i2] = silu2<FAST>(z[i2]);
     }
-    if (dvalid && ts + r < p.T) store_vec<T, CPT>(orow + r * D, z);
-#pragma unroll
-    for (int k = 0; k + 1 < PAD; ++k)
-#pragma unroll
-      for (int i2 = 0; i2 < NP; ++i2) xw[k][i2] = xw[k + 1][i2];
-#pragma unroll
-    for (int i2 = 0; i2 < NP; ++i2) xw[PAD - 1][i2] = xr[i2];
-  }
+    if (full_rows || (dvalid && ts + r < p.T)) store_vec<T, CPT>(orow + r * D, z);
+  });
 
   // final_states = last PAD rows of concat(initial_states, x) (causal_conv1d.py:153-164).
   if (p.final_states != nullptr && tt == p.n_tt - 1 && rg == 0 && dvalid) {
