@@ -192,8 +192,13 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
   const bool dvalid = d < p.D;
   const bool has_init = p.init != nullptr;
 
+  // With SiLU on 16-bit data the taps are halved: the step below computes h = z / 2 and carries
+  // dz2 = 2 dz, so w dz2 products equal the reference's w dz and dweight / dbias are halved once
+  // at the end (all exact power-of-two scalings).
+  constexpr bool HALF = SILU && FAST;
   float2 w[W][NP], bv[NP];
   load_taps<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, w, bv);
+  if constexpr (HALF) halve_taps<W, NP>(w, bv);
   float2 dw[W][NP], dbs[NP];
 #pragma unroll
   for (int i2 = 0; i2 < NP; ++i2) {
@@ -282,11 +287,15 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
 #pragma unroll
             for (int i2 = 0; i2 < NP; ++i2) {
               z[i2] = fadd2(z[i2], bv[i2]);
-              const float2 sg = sigmoid2<FAST>(z[i2]);
-              const float2 one = make_float2(1.f, 1.f);
-              const float2 oms = ffma2(sg, make_float2(-1.f, -1.f), one);
               // dz = dy * sig * (1 + z * (1 - sig))   (causal_conv1d.py:285-286)
-              dz[i2] = fmul2(fmul2(dz[i2], sg), ffma2(z[i2], oms, one));
+              if constexpr (HALF) {
+                dz[i2] = dsilu2_of_half(z[i2], dz[i2]);  // z holds h = z / 2; this is 2 dz
+              } else {
+                const float2 sg = sigmoid2<FAST>(z[i2]);
+                const float2 one = make_float2(1.f, 1.f);
+                const float2 oms = ffma2(sg, make_float2(-1.f, -1.f), one);
+                dz[i2] = fmul2(fmul2(dz[i2], sg), ffma2(z[i2], oms, one));
+              }
             }
           }
           if ((SEQ && seq_t < 0) || above) {
@@ -389,6 +398,15 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
     }
   });
 
+  if constexpr (HALF) {
+    const float2 half = make_float2(0.5f, 0.5f);
+#pragma unroll
+    for (int i2 = 0; i2 < NP; ++i2) {
+      dbs[i2] = fmul2(dbs[i2], half);
+#pragma unroll
+      for (int k = 0; k < W; ++k) dw[k][i2] = fmul2(dw[k][i2], half);
+    }
+  }
   // This thread's channels belong to this warp alone: write the partial sums directly.
   if (dvalid) {
     float* pp = p.partials + static_cast<int64_t>(part) * (W + 1) * D + d;

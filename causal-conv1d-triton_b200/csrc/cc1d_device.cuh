@@ -160,6 +160,25 @@ __device__ __forceinline__ float2 silu2(float2 z) {
   }
 }
 
+// The 16-bit (FAST) SiLU paths run on h = z / 2 directly: the kernels scale their fp32 taps and
+// bias by 0.5 once, which is exact in binary floating point, so the convolution yields h with the
+// bits of 0.5 * z. With t = tanh(h):
+//   SiLU(z)        = h + h t
+//   2 SiLU'(z)     = 1 + t + h (1 - t^2)      (= 2 sig (1 + z (1 - sig)), sig = (1 + t) / 2)
+// The backward multiplies dy by 2 SiLU'(z); the halved taps turn that back into dx exactly.
+__device__ __forceinline__ float2 tanh2(float2 h) { return make_float2(tanh_approx(h.x), tanh_approx(h.y)); }
+
+__device__ __forceinline__ float2 silu2_of_half(float2 h) { return ffma2(h, tanh2(h), h); }
+
+// dy * 2 SiLU'(z) from h = z / 2.
+__device__ __forceinline__ float2 dsilu2_of_half(float2 h, float2 dy) {
+  const float2 m1 = make_float2(-1.f, -1.f);
+  const float2 t = tanh2(h);
+  const float2 c = ffma2(t, t, m1);  // t^2 - 1
+  const float2 m = ffma2(h, c, m1);  // h (t^2 - 1) - 1
+  return fmul2(dy, ffma2(m, m1, t));  // dy (1 + t + h (1 - t^2))
+}
+
 // ---------------------------------------------------------------------------------------------
 // Conversions
 // ---------------------------------------------------------------------------------------------

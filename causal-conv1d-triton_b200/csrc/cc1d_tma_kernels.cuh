@@ -157,6 +157,18 @@ __device__ __forceinline__ void load_taps_fast(const void* weight, int w_dtype, 
   }
 }
 
+// Multiplies the taps and the bias by 0.5 (exact), for the kernels that compute h = z / 2.
+template <int W, int NP>
+__device__ __forceinline__ void halve_taps(float2 (&w)[W][NP], float2 (&bv)[NP]) {
+  const float2 half = make_float2(0.5f, 0.5f);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    bv[i] = fmul2(bv[i], half);
+#pragma unroll
+    for (int k = 0; k < W; ++k) w[k][i] = fmul2(w[k][i], half);
+  }
+}
+
 // Loads CPT channels of a row of a contiguous (B, W-1, D) state tensor (run-time dtype).
 template <int NP>
 __device__ __forceinline__ void load_state_row(const void* base, int dtype, int64_t row, int D, int d,
@@ -216,6 +228,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   const int64_t D = p.D;
   float2 w[W][NP], bv[NP];
   load_taps_fast<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, w, bv);
+  if constexpr (SILU && FAST) halve_taps<W, NP>(w, bv);  // z below is h = z / 2
   __syncthreads();  // barrier initialised, seq window written
   if (!mbar_wait(full, 0, p.status)) return;
 
@@ -268,7 +281,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
     }
     if constexpr (SILU) {
 #pragma unroll
-      for (int i2 = 0; i2 < NP; ++i2) z[i2] = silu2<FAST>(z[i2]);
+      for (int i2 = 0; i2 < NP; ++i2) z[i2] = FAST ? silu2_of_half(z[i2]) : silu2<false>(z[i2]);
     }
     if (full_rows || (dvalid && ts + r < p.T)) store_vec<T, CPT>(orow + r * D, z);
   });
