@@ -51,7 +51,7 @@ FALLBACK_HBM_GBS = 6650.0
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the backward kernel at
 # this workload (B=8, T=32768, D=1024, W=4, bias+SiLU), from the ncu launch list in
 # profiles/bwd_walk_kernel_cfg2.md; it scales with the B*T rows processed.
-BWD_DRAM_BYTES_PER_LAUNCH = 1090.6e6 + 510.0e6
+BWD_DRAM_BYTES_PER_LAUNCH = 1089.6e6 + 509.0e6
 BWD_DRAM_ROWS = 8 * 32768
 
 
