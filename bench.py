@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--sweep", action="store_true",
                     help="time every BASELINE config through both implementations' public APIs "
                          "(ours and the reference's Triton kernels) and print one JSON line each")
+    ap.add_argument("--decode", action="store_true",
+                    help="time the decode-time companions (causal_conv1d_update, "
+                         "seq_idx_from_cu_seqlens) and print one JSON line each")
     return ap.parse_args()
 
 
@@ -413,10 +416,108 @@ def run_sweep(args):
         torch.cuda.empty_cache()
 
 
+def _graph_us_per_call(fn, calls=100, reps=5):
+    """Device time per call of `fn` (no host sync inside), from replays of a CUDA graph holding
+    `calls` calls, so host launch overhead does not hide the kernel time; plus the eager host time
+    per call (launch-bound when the kernel is short)."""
+    import statistics as st
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(calls):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    dev_us = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        dev_us.append(e0.elapsed_time(e1) * 1e3 / calls)
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        fn()
+    torch.cuda.synchronize()
+    host_us = (time.perf_counter() - t0) * 1e6 / calls
+    del g
+    return st.median(dev_us), host_us
+
+
+def run_decode(args):
+    """Decode-time companions of the conv: the state update and the cu_seqlens front end.
+
+    causal_conv1d_update: one new row per sequence through the conv, the (slots, W-1, D) state read
+    and rewritten in place through a slot index, bias + SiLU, bf16 data and state, fp32 weights.
+    Algorithmic bytes per call: x and out rows (2 B each), the W-1 state rows read and written,
+    weight, bias and indices. seq_idx_from_cu_seqlens: cfg4's packed rows (B=4, T=16384, lengths
+    U[64, 4096]); bytes = the int32 seq_idx written + cu_seqlens read."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from causal_conv1d_b200 import causal_conv1d_update, seq_idx_from_cu_seqlens
+
+    peak, kind = measured_peak()
+    g = torch.Generator().manual_seed(0)
+    for name, B, D, W, slots in [("decode Mamba-2 conv dim (cfg4 D=4352, W=4), 256 sequences", 256, 4352, 4, 512),
+                                 ("decode cfg5 D=8192 W=8, 64 sequences", 64, 8192, 8, 128),
+                                 ("decode cfg2 D=1024 W=4, 8 sequences", 8, 1024, 4, 8)]:
+        x = torch.randn(B, D, generator=g).to(torch.bfloat16).to(dev)
+        state = torch.randn(slots, W - 1, D, generator=g).to(torch.bfloat16).to(dev)
+        idx = torch.randperm(slots, generator=g)[:B].to(torch.int32).to(dev)
+        w = (torch.randn(D, W, generator=g) * W ** -0.5).to(dev)
+        b = (torch.randn(D, generator=g) * 0.1 ** 0.5).to(dev)
+        dev_us, host_us = _graph_us_per_call(
+            lambda: causal_conv1d_update(x, state, w, b, activation="silu", conv_state_indices=idx))
+        nbytes = B * D * 2 * 2 + 2 * B * (W - 1) * D * 2 + D * W * 4 + D * 4 + B * 4
+        gbs = nbytes / (dev_us * 1e-6) / 1e9
+        print(json.dumps({"decode": name, "kernel": "cc1d_update_kernel", "batch": B, "dim": D, "width": W,
+                          "us_per_call": dev_us, "host_us_per_eager_call": host_us,
+                          "bytes_per_call": nbytes, "gbs": gbs, "frac_of_measured": gbs / peak,
+                          "peak": f"{kind} hbm_gbs {peak}", "timing": "CUDA graph of 100 calls, median of 5 replays"}),
+              flush=True)
+
+    B, T = 4, 16384
+    rows = []
+    for _ in range(B):
+        lens, tot = [], 0
+        while True:
+            n = int(torch.randint(64, 4097, (1,), generator=g))
+            if tot + n > T - int(torch.randint(0, 256, (1,), generator=g)):
+                break
+            lens.append(n)
+            tot += n
+        rows.append(lens)
+    n = max(len(r) for r in rows)
+    cu = torch.zeros(B, n + 1, dtype=torch.int32)
+    for i, r in enumerate(rows):  # rows with fewer sequences repeat their last boundary (empty seqs)
+        c = torch.tensor([0] + r).cumsum(0)
+        cu[i, :len(c)] = c
+        cu[i, len(c):] = c[-1]
+    cu = cu.to(dev)
+    dev_us, host_us = _graph_us_per_call(lambda: seq_idx_from_cu_seqlens(cu, T))
+    nbytes = B * T * 4 + cu.numel() * 4
+    gbs = nbytes / (dev_us * 1e-6) / 1e9
+    print(json.dumps({"decode": "seq_idx_from_cu_seqlens, cfg4 rows (B=4, T=16384)", "kernel": "cc1d_seq_idx_kernel",
+                      "n_seqs_per_row": n, "us_per_call": dev_us, "host_us_per_eager_call": host_us,
+                      "bytes_per_call": nbytes, "gbs": gbs, "frac_of_measured": gbs / peak,
+                      "timing": "CUDA graph of 100 calls, median of 5 replays"}), flush=True)
+
+
 def main():
     args = parse()
     if args.sweep:
         run_sweep(args)
+        return
+    if args.decode:
+        run_decode(args)
         return
     if args.impl == "reference":
         run_reference_cpu(args)

@@ -240,6 +240,28 @@ int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t sy
   return CC1D_OK;
 }
 
+template <typename T>
+const void* update_vec_for_width(int W) {
+  switch (W) {
+    case 2: return reinterpret_cast<const void*>(&cc1d_update_vec_kernel<T, 2>);
+    case 3: return reinterpret_cast<const void*>(&cc1d_update_vec_kernel<T, 3>);
+    case 4: return reinterpret_cast<const void*>(&cc1d_update_vec_kernel<T, 4>);
+    case 5: return reinterpret_cast<const void*>(&cc1d_update_vec_kernel<T, 5>);
+    case 6: return reinterpret_cast<const void*>(&cc1d_update_vec_kernel<T, 6>);
+    case 7: return reinterpret_cast<const void*>(&cc1d_update_vec_kernel<T, 7>);
+    case 8: return reinterpret_cast<const void*>(&cc1d_update_vec_kernel<T, 8>);
+    default: return nullptr;
+  }
+}
+
+// The vector decode kernel for x and state of one element type and widths 2..8, else null.
+const void* update_vec_kernel(int x_dtype, int state_dtype, int W) {
+  if (x_dtype != state_dtype) return nullptr;
+  if (x_dtype == kBF16) return update_vec_for_width<__nv_bfloat16>(W);
+  if (x_dtype == kF16) return update_vec_for_width<__half>(W);
+  return update_vec_for_width<float>(W);
+}
+
 }  // namespace
 }  // namespace cc1d
 
@@ -375,8 +397,19 @@ int cc1d_update(const void* x, int64_t stride_x_batch, int64_t stride_x_time, vo
   u.x_dtype = x_dtype, u.s_dtype = state_dtype, u.w_dtype = weight_dtype, u.b_dtype = bias_dtype, u.silu = silu != 0;
   const int64_t n = batch * dim;
   if (cdiv(n, 256) >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
-  cc1d_update_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0, static_cast<cudaStream_t>(stream_)>>>(u);
-  CC1D_TRY_CUDA(cudaGetLastError());
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const void* kernel = update_vec_kernel(x_dtype, state_dtype, static_cast<int>(width));
+  const int64_t cpt = x_dtype == kF32 ? 2 : 4;  // channels of one 8-byte vector
+  const bool vec = kernel != nullptr && dim % cpt == 0 && reinterpret_cast<uintptr_t>(x) % 8 == 0 &&
+                   reinterpret_cast<uintptr_t>(conv_state) % 8 == 0 && reinterpret_cast<uintptr_t>(out) % 8 == 0 &&
+                   stride_x_batch % cpt == 0 && stride_x_time % cpt == 0;
+  if (vec) {
+    void* args[] = {&u};
+    CC1D_TRY_CUDA(cudaLaunchKernel(kernel, dim3(static_cast<unsigned>(cdiv(n / cpt, 256))), dim3(256), args, 0, stream));
+  } else {
+    cc1d_update_kernel<<<static_cast<unsigned>(cdiv(n, 256)), 256, 0, stream>>>(u);
+    CC1D_TRY_CUDA(cudaGetLastError());
+  }
   return CC1D_OK;
 }
 

@@ -6,11 +6,17 @@
 //   window = concat(state[s, :, d], x[b, :, d])                     (W-1 + L values)
 //   out[b, l, d] = act(bias[d] + sum_k w[d, k] window[l + k])       in the forward's order
 //   state[s, p, d] = window[L + p]                                  (p < W-1), in place
-// One thread per (b, d), so a warp reads and writes 32 consecutive channels. Element types are
-// run-time values: decode is latency-bound, not arithmetic-bound.
+// Two kernels. cc1d_update_vec_kernel<T, W> (widths 2..8, x and state of one type T, D a multiple
+// of the vector's channels, 8-byte aligned rows) gives each thread one 8-byte vector of channels
+// (4 bf16/fp16, 2 fp32): it loads its W-1 state rows and each new x row as one vector each, keeps
+// the window in registers, and writes the outputs and the new state rows once, so a thread makes
+// one round trip to memory and a 256-sequence batch of a Mamba-2 layer fits in one resident wave.
+// cc1d_update_kernel covers every other case (run-time width and element types, one thread per
+// (b, d)).
 #pragma once
 
 #include "cc1d_device.cuh"
+#include "cc1d_tma_kernels.cuh"  // load_taps_fast
 
 namespace cc1d {
 
@@ -54,6 +60,50 @@ __global__ void __launch_bounds__(256) cc1d_update_kernel(const UpdateParams p) 
   // New state: entry q takes window[L + q]. Walking q upwards, entry q is written only after the
   // entry it may still need (old entry q + L > q) has been read.
   for (int q = 0; q < PAD; ++q) st_any(p.state, sbase + static_cast<int64_t>(q) * p.D, p.s_dtype, window(p.L + q));
+}
+
+template <typename T, int W>
+__global__ void __launch_bounds__(256) cc1d_update_vec_kernel(const UpdateParams p) {
+  constexpr int CPT = 8 / static_cast<int>(sizeof(T));  // one 8-byte vector: 4 bf16/fp16 or 2 fp32
+  constexpr int NP = CPT / 2, PAD = W - 1;
+  constexpr bool FAST = sizeof(T) == 2;
+  const int DV = p.D / CPT;
+  const int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (idx >= static_cast<int64_t>(p.B) * DV) return;
+  const int b = static_cast<int>(idx / DV), d = CPT * static_cast<int>(idx - static_cast<int64_t>(b) * DV);
+  const int64_t srow = p.indices != nullptr ? p.indices[b] : b;
+  if (srow < 0) return;  // a padded batch entry
+  T* st = static_cast<T*>(p.state) + srow * PAD * p.D + d;
+  const T* xb = static_cast<const T*>(p.x) + b * p.sxb + d;
+  T* ob = static_cast<T*>(p.out) + static_cast<int64_t>(b) * p.L * p.D + d;
+
+  float2 win[PAD][NP];  // win[k] = the input PAD - k rows before the next one
+#pragma unroll
+  for (int q = 0; q < PAD; ++q) load_vec<T, CPT>(st + static_cast<int64_t>(q) * p.D, win[q]);
+  float2 w[W][NP], bv[NP];
+  load_taps_fast<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, true, w, bv);
+  for (int l = 0; l < p.L; ++l) {
+    float2 xr[NP], z[NP];
+    load_vec<T, CPT>(xb + static_cast<int64_t>(l) * p.sxt, xr);
+    // The forward's per-element order (causal_conv1d.py:129-143).
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+      z[i] = fmul2(w[PAD][i], xr[i]);
+#pragma unroll
+      for (int k = 0; k < PAD; ++k) z[i] = ffma2(w[k][i], win[k][i], z[i]);
+      z[i] = fadd2(z[i], bv[i]);
+      if (p.silu) z[i] = silu2<FAST>(z[i]);
+    }
+    store_vec<T, CPT>(ob + static_cast<int64_t>(l) * p.D, z);
+#pragma unroll
+    for (int i = 0; i < NP; ++i) {
+#pragma unroll
+      for (int k = 0; k + 1 < PAD; ++k) win[k][i] = win[k + 1][i];
+      win[PAD - 1][i] = xr[i];
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < PAD; ++q) store_vec<T, CPT>(st + static_cast<int64_t>(q) * p.D, win[q]);
 }
 
 }  // namespace cc1d

@@ -77,6 +77,32 @@ def test_update_fp32_no_activation():
     assert_bitexact(sd.cpu(), rs, "state")
 
 
+@pytest.mark.parametrize("case", ["odd_dim", "dim_6_mod_4", "fp32_state", "odd_row_stride", "vec_path"])
+def test_update_paths_match_oracle(case):
+    """The vector decode kernel (D and the strides multiples of 4 bf16 channels, x and state of one
+    type) and the general one (every other case) give the oracle's results."""
+    from causal_conv1d_b200 import causal_conv1d_update
+
+    g = torch.Generator().manual_seed(len(case))
+    B, L, W = 3, 4, 4
+    D = {"odd_dim": 37, "dim_6_mod_4": 66}.get(case, 64)
+    sdt = torch.float32 if case == "fp32_state" else torch.bfloat16
+    x = torch.randn(B, L, D, generator=g).to(torch.bfloat16)
+    w = torch.randn(D, W, generator=g) / W**0.5
+    b = torch.randn(D, generator=g) * 0.3
+    st = torch.randn(B, W - 1, D, generator=g).to(sdt)
+    xd = x.to(DEV)
+    if case == "odd_row_stride":  # x read as a column slice of a wider buffer: row stride D + 1
+        wide = torch.zeros(B, L, D + 1, dtype=torch.bfloat16, device=DEV)
+        wide[..., 1:] = xd
+        xd = wide[..., 1:]
+    sd = st.to(DEV)
+    out = causal_conv1d_update(xd, sd, w.to(DEV), b.to(DEV), activation="silu").cpu()
+    ro, rs = oracle.update(x, st.float(), w, b, silu=True)
+    assert_close(out, torch.from_numpy(ro).to(torch.bfloat16).float(), "bf16", "out")
+    assert_bitexact(sd.cpu().float(), torch.from_numpy(rs).to(sdt).float(), "state")
+
+
 def _seq_idx_reference(cu, T):
     out = np.full(T, -1, np.int32)
     for i in range(len(cu) - 1):
