@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--sweep", action="store_true",
                     help="time every BASELINE config through both implementations' public APIs "
                          "(ours and the reference's Triton kernels) and print one JSON line each")
+    ap.add_argument("--fusion", action="store_true",
+                    help="time split_conv1d (the conv fused with a Mamba-2 block's splits) against "
+                         "torch.split around causal_conv1d_fn, forward + backward, at cfg4's shape")
     ap.add_argument("--decode", action="store_true",
                     help="time the decode-time companions (causal_conv1d_update, "
                          "seq_idx_from_cu_seqlens) and print one JSON line each")
@@ -511,10 +514,82 @@ def run_decode(args):
                       "timing": "CUDA graph of 100 calls, median of 5 replays"}), flush=True)
 
 
+def run_fusion(args):
+    """split_conv1d against the unfused Mamba-2 composition at BASELINE config 4's shape.
+
+    zxbcdt (B=4, T=16384, 4096 + 4352 + 64 channels) bf16: z (d_inner 4096), xBC (x 4096, B 128,
+    C 128: cfg4's D=4352 conv dim) and dt (64 heads). Bias + SiLU, cfg4's packed seq_idx and
+    initial states. One step = forward and backward through autograd with fixed upstream gradients
+    for z, x, B, C and dt (separate tensors, as the SSM produces them). The unfused step
+    concatenates the x/B/C gradients into dout and then dz, dxBC and ddt into d(zxbcdt); the fused
+    step does neither (bytes avoided: 4 x B*T*D_xbc*2)."""
+    import statistics as st
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from causal_conv1d_b200 import causal_conv1d_fn, split_conv1d
+
+    B, T, d_z, split, d_dt, W = 4, 16384, 4096, (4096, 128, 128), 64, 4
+    d_xbc = sum(split)
+    g = torch.Generator().manual_seed(0)
+    zx = torch.randn(B, T, d_z + d_xbc + d_dt, generator=g).to(torch.bfloat16).to(dev).requires_grad_(True)
+    w = (torch.randn(d_xbc, W, generator=g) * 0.5).to(dev).requires_grad_(True)
+    b = (torch.randn(d_xbc, generator=g) * 0.1 ** 0.5).to(dev).requires_grad_(True)
+    init = torch.randn(B, W - 1, d_xbc, generator=g).to(torch.bfloat16).to(dev).requires_grad_(True)
+    seq = torch.empty(B, T, dtype=torch.int32)
+    for r in range(B):
+        t, i = 0, 0
+        pad = int(torch.randint(0, 256, (1,), generator=g))
+        while t < T - pad:
+            n = min(int(torch.randint(64, 4097, (1,), generator=g)), T - pad - t)
+            seq[r, t:t + n] = i
+            t, i = t + n, i + 1
+        seq[r, T - pad:] = -1
+    seq = seq.to(dev)
+    widths = [d_z, *split, d_dt]
+    ups = [torch.randn(B, T, c, generator=g).to(torch.bfloat16).to(dev) for c in widths]
+
+    def fused():
+        outs = split_conv1d(zx, w, b, d_z=d_z, xbc_split=split, seq_idx=seq, initial_states=init,
+                            activation="silu")
+        torch.autograd.backward(outs, ups)
+
+    def unfused():
+        z, xbc, dtp = zx.split([d_z, d_xbc, d_dt], dim=-1)
+        y = causal_conv1d_fn(xbc, w, b, seq_idx=seq, initial_states=init, activation="silu")
+        torch.autograd.backward((z, *y.split(list(split), dim=-1), dtp), ups)
+
+    res = {"fused": [], "unfused": []}
+    for _ in range(3):
+        fused(), unfused()
+    for _ in range(7):
+        for name, fn in (("fused", fused), ("unfused", unfused)):
+            for t in (zx, w, b, init):
+                t.grad = None
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            res[name].append(e0.elapsed_time(e1) / 5 * 1e3)
+    f, u = st.median(res["fused"]), st.median(res["unfused"])
+    print(json.dumps({"fusion": "split_conv1d vs torch.split + causal_conv1d_fn + split, fwd + bwd",
+                      "shape": {"batch": B, "seqlen": T, "d_z": d_z, "xbc_split": list(split), "d_dt": d_dt,
+                                "width": W, "seq_idx": "cfg4 packed", "initial_states": True},
+                      "fused_us": f, "unfused_us": u, "speedup": u / f,
+                      "bytes_avoided_per_step": 4 * B * T * d_xbc * 2,
+                      "timing": "CUDA events, 5 steps per sample, median of 7 interleaved samples"}),
+          flush=True)
+
+
 def main():
     args = parse()
     if args.sweep:
         run_sweep(args)
+        return
+    if args.fusion:
+        run_fusion(args)
         return
     if args.decode:
         run_decode(args)

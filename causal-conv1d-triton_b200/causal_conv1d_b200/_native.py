@@ -23,6 +23,16 @@ CC1D_ERR_UNSUPPORTED = 2
 CC1D_ERR_WORKSPACE = 3
 CC1D_ERR_CUDA = 4
 CC1D_ERR_SCRATCH_LIMIT = 5
+CC1D_ERR_LAYOUT = 6
+CC1D_MAX_DOUT_PIECES = 4
+
+
+class DoutPiece(ctypes.Structure):
+    """cc1d_dout_piece: one channel range of dout in its own tensor."""
+
+    _fields_ = [("ptr", ctypes.c_void_p), ("stride_batch", ctypes.c_int64),
+                ("stride_time", ctypes.c_int64), ("channels", ctypes.c_int64)]
+
 
 # Every symbol the header declares, with its ctypes signature.
 _P, _I64, _I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
@@ -39,6 +49,10 @@ SIGNATURES = {
                   _P, _I64, _I64, _I64, _I64, _I64, _I, _I, _I, _I, _I, _P], _I),
     "cc1d_bwd_noalloc": ([_P, _I64, _I64, _P, _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P, _P,
                           _I64, _I64, _I64, _I64, _I, _I, _I, _I, _I, _P], _I),
+    "cc1d_bwd_split": ([_P, _I64, _I64, _P, _P, _P, _P, ctypes.POINTER(DoutPiece), _I, _P, _P, _I64,
+                        _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _I, _I, _I,
+                        _I, _P], _I),
+    "cc1d_copy_channels": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I, _P], _I),
     "cc1d_status": ([ctypes.POINTER(ctypes.c_uint32), _I], _I),
     "cc1d_error_string": ([_I], ctypes.c_char_p),
     "cc1d_last_cuda_error": ([], _I),

@@ -153,6 +153,72 @@ def _bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_din
     return dx, dweight, dbias, dinit
 
 
+def _copy_channels(dst, src):
+    """dst[...] = src for two (B, T, C) tensors with channel stride 1 and any batch/time strides,
+    through the library's vectorised copy (cc1d_copy_channels)."""
+    assert dst.shape == src.shape and dst.dtype == src.dtype and dst.dim() == 3
+    if src.stride(2) != 1:
+        src = src.contiguous()
+    assert dst.stride(2) == 1
+    B, T, C = dst.shape
+    with _DeviceGuard(dst.device):
+        check(lib.cc1d_copy_channels(dst.data_ptr(), dst.stride(0), dst.stride(1), src.data_ptr(), src.stride(0),
+                                     src.stride(1), B, T, C, dst.element_size(), _stream(dst.device)),
+              "cc1d_copy_channels")
+
+
+def _bwd_split(x, weight, bias, seq_idx, initial_states, dout_pieces, need_dinit, silu, dx):
+    """Backward with dout given as channel pieces and dx written into a caller's view.
+
+    dout_pieces: (B, T, w_i) tensors with channel stride 1 whose widths sum to D, in channel order
+    (at most CC1D_MAX_DOUT_PIECES). dx: a (B, T, D) view with channel stride 1 (for instance a
+    channel slice of a wider gradient buffer), written in place. Returns (dweight, dbias, dinit).
+    Uses cc1d_bwd_split, which reads the pieces where they lie and writes dx at its strides; when
+    the layout is outside its fast path (CC1D_ERR_LAYOUT, reported before any device work) the
+    pieces are concatenated and the ordinary backward runs, with dx copied into place.
+    """
+    B, T, D = x.shape
+    W = weight.shape[1]
+    assert sum(p.shape[-1] for p in dout_pieces) == D and dx.shape == (B, T, D) and dx.stride(2) == 1
+    if len(dout_pieces) <= _native.CC1D_MAX_DOUT_PIECES:
+        dinit = torch.empty_like(initial_states) if need_dinit else None
+        w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
+        dinit_k = _as_float(dinit)
+        dweight = torch.empty_like(w)
+        dbias = torch.empty_like(b) if b is not None else None
+        p0 = dout_pieces[0]
+        with _DeviceGuard(x.device):
+            ws_bytes = lib.cc1d_bwd_workspace_bytes(
+                x.data_ptr(), x.stride(0), x.stride(1), p0.data_ptr(), p0.stride(0), p0.stride(1),
+                B, T, D, W, DTYPE_CODE[x.dtype],
+            )
+            if ws_bytes < 0:
+                check(_native.CC1D_ERR_INVALID, "causal_conv1d backward workspace")
+            workspace = torch.empty(max(1, ws_bytes // 4), device=x.device, dtype=torch.float32)
+            pieces = (_native.DoutPiece * len(dout_pieces))(
+                *[_native.DoutPiece(p.data_ptr(), p.stride(0), p.stride(1), p.shape[2]) for p in dout_pieces])
+            rc = lib.cc1d_bwd_split(
+                x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init), _ptr(seq_idx),
+                pieces, len(dout_pieces), None, dx.data_ptr(), dx.stride(0), dx.stride(1), _ptr(dweight),
+                _ptr(dbias), _ptr(dinit_k), None, workspace.data_ptr(), ws_bytes, B, T, D, W,
+                DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
+                _stream(x.device),
+            )
+        if rc != _native.CC1D_ERR_LAYOUT:
+            check(rc, "causal_conv1d split backward")
+            if dinit is not None and dinit_k is not dinit:
+                dinit.copy_(dinit_k)
+            if dweight.dtype != weight.dtype:
+                dweight = dweight.to(weight.dtype)
+            if dbias is not None and dbias.dtype != bias.dtype:
+                dbias = dbias.to(bias.dtype)
+            return dweight, dbias, dinit
+    dout = torch.cat([p.contiguous() for p in dout_pieces], dim=-1)
+    dx_full, dweight, dbias, dinit = _bwd(x, weight, bias, seq_idx, initial_states, dout, None, need_dinit, silu)
+    dx.copy_(dx_full)
+    return dweight, dbias, dinit
+
+
 class _CausalConv1dFn(torch.autograd.Function):
     """Autograd wrapper (the reference's `_CausalConv1dFn`, causal_conv1d.py:544-576)."""
 

@@ -14,8 +14,11 @@
 #include "cc1d_reduce_kernels.cuh"
 #include "cc1d_seqidx_kernel.cuh"
 #include "cc1d_update_kernel.cuh"
+#include "cc1d_copy_kernel.cuh"
 
 namespace cc1d {
+
+static_assert(kMaxDoutPieces == CC1D_MAX_DOUT_PIECES, "one limit on dout pieces");
 
 __device__ unsigned g_status_word;
 
@@ -265,11 +268,156 @@ const void* update_vec_kernel(int x_dtype, int state_dtype, int W) {
 }  // namespace
 }  // namespace cc1d
 
+namespace cc1d {
+namespace {
+
+// The backward behind cc1d_bwd (one dout piece, contiguous dx) and cc1d_bwd_split (dout as channel
+// pieces, dx at strides; TMA path required, else CC1D_ERR_LAYOUT before any device work).
+int bwd_impl(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* weight, const void* bias,
+             const void* initial_states, const int32_t* seq_idx, const cc1d_dout_piece* pieces, int n_pieces,
+             const void* dfinal_states, void* dx, int64_t stride_dx_batch, int64_t stride_dx_time, void* dweight,
+             void* dbias, void* dinit, float* grad_f32, void* workspace, int64_t workspace_bytes, int64_t batch,
+             int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype, int bias_dtype,
+             int init_dtype, int silu, void* stream_, bool split) {
+  const void* dout = pieces[0].ptr;
+  const int64_t stride_dout_batch = pieces[0].stride_batch, stride_dout_time = pieces[0].stride_time;
+  if (!valid_dtype(x_dtype) || !valid_dtype(weight_dtype) || (bias && !valid_dtype(bias_dtype)) ||
+      (initial_states && !valid_dtype(init_dtype)))
+    return CC1D_ERR_INVALID;
+  if (dinit != nullptr && initial_states == nullptr) return CC1D_ERR_INVALID;
+  if (grad_f32 == nullptr && dweight == nullptr) return CC1D_ERR_INVALID;
+  CC1D_TRY(check_sizes(batch, seqlen, dim, width));
+  if (batch == 0 || dim == 0) return CC1D_OK;
+  const int64_t B = batch, T = seqlen, D = dim, W = width, PAD = W - 1;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DeviceInfo di;
+  int dev = 0;
+  CC1D_TRY(device_info(&di, &dev));
+  if (T == 0) {  // dinit = dfinal (or zero); no output rows, so dweight = dbias = 0
+    if (dinit) CC1D_TRY(launch_fill(dinit, init_dtype, dfinal_states, x_dtype, B * PAD * D, di.sms, stream));
+    if (grad_f32) {
+      CC1D_TRY(launch_fill(grad_f32, kF32, nullptr, kF32, (W + 1) * D, di.sms, stream));
+    } else {
+      CC1D_TRY(launch_fill(dweight, weight_dtype, nullptr, kF32, W * D, di.sms, stream));
+      if (bias && dbias) CC1D_TRY(launch_fill(dbias, bias_dtype, nullptr, kF32, D, di.sms, stream));
+    }
+    return CC1D_OK;
+  }
+  if (!x || !weight || !dout || !dx) return CC1D_ERR_INVALID;
+
+  BwdPlan pl;
+  CC1D_TRY(plan_bwd(x, stride_x_batch, stride_x_time, dout, stride_dout_batch, stride_dout_time, B, T, D, W, x_dtype,
+                    seq_idx != nullptr, silu != 0, di, dev, &pl));
+  if (split) {
+    // Every piece and dx must suit the TMA walk: piece boundaries on channel blocks, 16-byte
+    // aligned bases and strides (dx is written as 8-byte vectors at these strides).
+    const int es = elem_size(x_dtype);
+    bool ok = pl.tma && reinterpret_cast<uintptr_t>(dx) % 16 == 0 && stride_dx_time >= D &&
+              (stride_dx_time * es) % 16 == 0 && (B == 1 || (stride_dx_batch * es) % 16 == 0);
+    int64_t c0 = 0;
+    for (int i = 0; ok && i < n_pieces; ++i) {
+      ok = c0 % pl.k.box_d == 0 &&
+           tma_layout_ok(pieces[i].ptr, pieces[i].stride_batch, pieces[i].stride_time, B, pieces[i].channels, es);
+      c0 += pieces[i].channels;
+    }
+    if (!ok) return CC1D_ERR_LAYOUT;
+  }
+  if (workspace == nullptr || workspace_bytes < pl.ws_bytes) return CC1D_ERR_WORKSPACE;
+  float* partials = static_cast<float*>(workspace);
+
+  bool launched = false;
+  if (pl.tma) {
+    BwdWalkParams p{};
+    const int PADi = static_cast<int>(PAD);
+    const int box_d = pl.k.box_d;  // one channel block per consumer warp
+    bool maps = encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, box_d, pl.k.t_tile + PADi);
+    int64_t c_end = 0;
+    for (int i = 0; maps && i < n_pieces; ++i) {
+      maps = encode_3d(&p.tmap_dy[i], pieces[i].ptr, x_dtype, B, T, pieces[i].channels, pieces[i].stride_batch,
+                       pieces[i].stride_time, box_d, pl.k.t_tile);
+      c_end += pieces[i].channels;
+      p.dy_end[i] = static_cast<int>(c_end);
+    }
+    p.n_dy = n_pieces;
+    p.sdxb = stride_dx_batch, p.sdxt = stride_dx_time;
+    if (!maps && split) return CC1D_ERR_LAYOUT;
+    if (maps) {
+      int occ = 0;
+      CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
+      p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
+      p.dfinal = dfinal_states, p.dx = dx, p.dinit = dinit, p.partials = partials, p.status = di.status;
+      p.rows_per_part = pl.rows_per_part;
+      p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D);
+      p.n_groups = pl.n_blk;
+      p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
+      void* args[] = {&p};
+      CC1D_TRY_CUDA(
+          cudaLaunchKernel(pl.k.fn, dim3(static_cast<unsigned>(pl.grid)), dim3(pl.k.threads), args, pl.k.smem, stream));
+      launched = true;
+    }
+  }
+  if (!launched) {
+    if (split) return CC1D_ERR_LAYOUT;  // unreachable: the split call requires the TMA path
+    // The tensor maps could not be encoded: re-plan on the generic path, whose partial count is
+    // never larger than the TMA path's, so the workspace still suffices.
+    if (pl.tma) {
+      const int64_t ws_tma = pl.ws_bytes;
+      pl.tma = false;
+      pl.k = bwd_generic_for(x_dtype, static_cast<int>(W));
+      pl.max_smem = generic_bwd_smem(kGenericMaxWidth);
+      int occ = 0;
+      CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
+      pl.n_blk = static_cast<int>(cdiv(D, pl.k.d_tile));
+      pl.n_tt = static_cast<int>(cdiv(T, pl.k.t_tile));
+      const int64_t M = B * pl.n_tt;
+      const int64_t cap = static_cast<int64_t>(di.sms) * occ;
+      const int64_t pmax = std::max<int64_t>(1, ws_tma / ((W + 1) * D * 4));
+      pl.P = static_cast<int>(std::max<int64_t>(1, std::min({M, cap / pl.n_blk, pmax})));
+      pl.grid = static_cast<int64_t>(pl.P) * pl.n_blk;
+    }
+    int occ = 0;
+    CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
+    GenericParams g{};
+    g.x = x, g.weight = weight, g.bias = bias, g.init = initial_states, g.seq = seq_idx;
+    g.dy = dout, g.dfinal = dfinal_states, g.dx = dx, g.dinit = dinit, g.partials = partials, g.status = di.status;
+    g.sxb = stride_x_batch, g.sxt = stride_x_time, g.syb = stride_dout_batch, g.syt = stride_dout_time;
+    g.B = static_cast<int>(B), g.T = static_cast<int>(T), g.D = static_cast<int>(D), g.W = static_cast<int>(W);
+    g.n_tt = pl.n_tt, g.n_dc = pl.n_blk;
+    g.w_dtype = weight_dtype, g.b_dtype = bias_dtype, g.init_dtype = init_dtype, g.silu = silu != 0;
+    void* args[] = {&g};
+    CC1D_TRY_CUDA(
+        cudaLaunchKernel(pl.k.fn, dim3(static_cast<unsigned>(pl.grid)), dim3(pl.k.threads), args, pl.k.smem, stream));
+  }
+
+  // Second stage: fixed-order sum over the P partial rows (32 column groups x 32 row slices per block).
+  const int64_t N = (W + 1) * D;
+  const bool vec4 = N % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0;
+  const int64_t groups = vec4 ? N / 4 : N;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(cdiv(groups, kReduceCols), 65535)));
+  const int rthreads = kReduceCols * kReduceSlices;
+  if (vec4)
+    cc1d_reduce_partials_kernel<4><<<blocks, rthreads, 0, stream>>>(partials, pl.P, static_cast<int>(D),
+                                                                    static_cast<int>(W), dweight, weight_dtype,
+                                                                    bias ? dbias : nullptr, bias_dtype, grad_f32,
+                                                                    bias != nullptr);
+  else
+    cc1d_reduce_partials_kernel<1><<<blocks, rthreads, 0, stream>>>(partials, pl.P, static_cast<int>(D),
+                                                                    static_cast<int>(W), dweight, weight_dtype,
+                                                                    bias ? dbias : nullptr, bias_dtype, grad_f32,
+                                                                    bias != nullptr);
+  CC1D_TRY_CUDA(cudaGetLastError());
+  return CC1D_OK;
+}
+
+
+}  // namespace
+}  // namespace cc1d
+
 using namespace cc1d;
 
 extern "C" {
 
-int cc1d_abi_version(void) { return 1; }
+int cc1d_abi_version(void) { return 2; }
 
 const char* cc1d_error_string(int code) {
   switch (code) {
@@ -280,6 +428,8 @@ const char* cc1d_error_string(int code) {
     case CC1D_ERR_CUDA: return "CUDA call failed (see cc1d_last_cuda_error())";
     case CC1D_ERR_SCRATCH_LIMIT:
       return "backward needs more scratch than cc1d_bwd_noalloc's fixed 8 MiB buffer; call cc1d_bwd with a workspace";
+    case CC1D_ERR_LAYOUT:
+      return "cc1d_bwd_split: dout pieces or dx strides outside the TMA path; concatenate dout and call cc1d_bwd";
     default: return "unknown error";
   }
 }
@@ -413,6 +563,42 @@ int cc1d_update(const void* x, int64_t stride_x_batch, int64_t stride_x_time, vo
   return CC1D_OK;
 }
 
+int cc1d_copy_channels(void* dst, int64_t dst_stride_batch, int64_t dst_stride_time, const void* src,
+                       int64_t src_stride_batch, int64_t src_stride_time, int64_t batch, int64_t seqlen,
+                       int64_t channels, int elem_bytes, void* stream_) {
+  if (batch < 0 || seqlen < 0 || channels < 0 || (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 &&
+                                                  elem_bytes != 8))
+    return CC1D_ERR_INVALID;
+  if (batch == 0 || seqlen == 0 || channels == 0) return CC1D_OK;
+  if (!dst || !src) return CC1D_ERR_INVALID;
+  CopyParams c{};
+  c.src = static_cast<const unsigned char*>(src), c.dst = static_cast<unsigned char*>(dst);
+  c.src_sb = src_stride_batch * elem_bytes, c.src_st = src_stride_time * elem_bytes;
+  c.dst_sb = dst_stride_batch * elem_bytes, c.dst_st = dst_stride_time * elem_bytes;
+  c.T = seqlen, c.rows = batch * seqlen;
+  const int64_t row_bytes = channels * elem_bytes;
+  uint64_t g = static_cast<uint64_t>(row_bytes) | reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) |
+               static_cast<uint64_t>(c.src_st) | static_cast<uint64_t>(c.dst_st);
+  if (batch > 1) g |= static_cast<uint64_t>(c.src_sb) | static_cast<uint64_t>(c.dst_sb);
+  const int vb = g % 16 == 0 ? 16 : g % 8 == 0 ? 8 : g % 4 == 0 ? 4 : g % 2 == 0 ? 2 : 0;
+  if (vb == 0) return CC1D_ERR_INVALID;  // single bytes: not a channel block of this library's types
+  c.vpr = row_bytes / vb;
+  DeviceInfo di;
+  int dev = 0;
+  CC1D_TRY(device_info(&di, &dev));
+  const int64_t n = c.rows * c.vpr;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(cdiv(n, 256), int64_t(di.sms) * 16));
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  switch (vb) {
+    case 16: cc1d_copy_channels_kernel<16><<<blocks, 256, 0, stream>>>(c); break;
+    case 8: cc1d_copy_channels_kernel<8><<<blocks, 256, 0, stream>>>(c); break;
+    case 4: cc1d_copy_channels_kernel<4><<<blocks, 256, 0, stream>>>(c); break;
+    default: cc1d_copy_channels_kernel<2><<<blocks, 256, 0, stream>>>(c); break;
+  }
+  CC1D_TRY_CUDA(cudaGetLastError());
+  return CC1D_OK;
+}
+
 int64_t cc1d_bwd_workspace_bytes(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* dout,
                                  int64_t stride_dout_batch, int64_t stride_dout_time, int64_t batch, int64_t seqlen,
                                  int64_t dim, int64_t width, int x_dtype) {
@@ -433,107 +619,30 @@ int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
              int64_t stride_dout_time, const void* dfinal_states, void* dx, void* dweight, void* dbias, void* dinit,
              float* grad_f32, void* workspace, int64_t workspace_bytes, int64_t batch, int64_t seqlen, int64_t dim,
              int64_t width, int x_dtype, int weight_dtype, int bias_dtype, int init_dtype, int silu, void* stream_) {
-  if (!valid_dtype(x_dtype) || !valid_dtype(weight_dtype) || (bias && !valid_dtype(bias_dtype)) ||
-      (initial_states && !valid_dtype(init_dtype)))
-    return CC1D_ERR_INVALID;
-  if (dinit != nullptr && initial_states == nullptr) return CC1D_ERR_INVALID;
-  if (grad_f32 == nullptr && dweight == nullptr) return CC1D_ERR_INVALID;
-  CC1D_TRY(check_sizes(batch, seqlen, dim, width));
-  if (batch == 0 || dim == 0) return CC1D_OK;
-  const int64_t B = batch, T = seqlen, D = dim, W = width, PAD = W - 1;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-  DeviceInfo di;
-  int dev = 0;
-  CC1D_TRY(device_info(&di, &dev));
-  if (T == 0) {  // dinit = dfinal (or zero); no output rows, so dweight = dbias = 0
-    if (dinit) CC1D_TRY(launch_fill(dinit, init_dtype, dfinal_states, x_dtype, B * PAD * D, di.sms, stream));
-    if (grad_f32) {
-      CC1D_TRY(launch_fill(grad_f32, kF32, nullptr, kF32, (W + 1) * D, di.sms, stream));
-    } else {
-      CC1D_TRY(launch_fill(dweight, weight_dtype, nullptr, kF32, W * D, di.sms, stream));
-      if (bias && dbias) CC1D_TRY(launch_fill(dbias, bias_dtype, nullptr, kF32, D, di.sms, stream));
-    }
-    return CC1D_OK;
-  }
-  if (!x || !weight || !dout || !dx) return CC1D_ERR_INVALID;
+  const cc1d_dout_piece piece{dout, stride_dout_batch, stride_dout_time, dim};
+  return bwd_impl(x, stride_x_batch, stride_x_time, weight, bias, initial_states, seq_idx, &piece, 1, dfinal_states, dx,
+                  seqlen * dim, dim, dweight, dbias, dinit, grad_f32, workspace, workspace_bytes, batch, seqlen, dim,
+                  width, x_dtype, weight_dtype, bias_dtype, init_dtype, silu, stream_, false);
+}
 
-  BwdPlan pl;
-  CC1D_TRY(plan_bwd(x, stride_x_batch, stride_x_time, dout, stride_dout_batch, stride_dout_time, B, T, D, W, x_dtype,
-                    seq_idx != nullptr, silu != 0, di, dev, &pl));
-  if (workspace == nullptr || workspace_bytes < pl.ws_bytes) return CC1D_ERR_WORKSPACE;
-  float* partials = static_cast<float*>(workspace);
-
-  bool launched = false;
-  if (pl.tma) {
-    BwdWalkParams p{};
-    const int PADi = static_cast<int>(PAD);
-    const int box_d = pl.k.box_d;  // one channel block per consumer warp
-    if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, box_d, pl.k.t_tile + PADi) &&
-        encode_3d(&p.tmap_dy, dout, x_dtype, B, T, D, stride_dout_batch, stride_dout_time, box_d, pl.k.t_tile)) {
-      int occ = 0;
-      CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
-      p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
-      p.dfinal = dfinal_states, p.dx = dx, p.dinit = dinit, p.partials = partials, p.status = di.status;
-      p.rows_per_part = pl.rows_per_part;
-      p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D);
-      p.n_groups = pl.n_blk;
-      p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
-      void* args[] = {&p};
-      CC1D_TRY_CUDA(
-          cudaLaunchKernel(pl.k.fn, dim3(static_cast<unsigned>(pl.grid)), dim3(pl.k.threads), args, pl.k.smem, stream));
-      launched = true;
-    }
+int cc1d_bwd_split(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* weight,
+                   const void* bias, const void* initial_states, const int32_t* seq_idx,
+                   const cc1d_dout_piece* dout_pieces, int n_pieces, const void* dfinal_states, void* dx,
+                   int64_t stride_dx_batch, int64_t stride_dx_time, void* dweight, void* dbias, void* dinit,
+                   float* grad_f32, void* workspace, int64_t workspace_bytes, int64_t batch, int64_t seqlen,
+                   int64_t dim, int64_t width, int x_dtype, int weight_dtype, int bias_dtype, int init_dtype,
+                   int silu, void* stream_) {
+  if (dout_pieces == nullptr || n_pieces < 1 || n_pieces > kMaxDoutPieces) return CC1D_ERR_INVALID;
+  int64_t sum = 0;
+  for (int i = 0; i < n_pieces; ++i) {
+    if (dout_pieces[i].channels <= 0) return CC1D_ERR_INVALID;
+    sum += dout_pieces[i].channels;
   }
-  if (!launched) {
-    // The tensor maps could not be encoded: re-plan on the generic path, whose partial count is
-    // never larger than the TMA path's, so the workspace still suffices.
-    if (pl.tma) {
-      const int64_t ws_tma = pl.ws_bytes;
-      pl.tma = false;
-      pl.k = bwd_generic_for(x_dtype, static_cast<int>(W));
-      pl.max_smem = generic_bwd_smem(kGenericMaxWidth);
-      int occ = 0;
-      CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
-      pl.n_blk = static_cast<int>(cdiv(D, pl.k.d_tile));
-      pl.n_tt = static_cast<int>(cdiv(T, pl.k.t_tile));
-      const int64_t M = B * pl.n_tt;
-      const int64_t cap = static_cast<int64_t>(di.sms) * occ;
-      const int64_t pmax = std::max<int64_t>(1, ws_tma / ((W + 1) * D * 4));
-      pl.P = static_cast<int>(std::max<int64_t>(1, std::min({M, cap / pl.n_blk, pmax})));
-      pl.grid = static_cast<int64_t>(pl.P) * pl.n_blk;
-    }
-    int occ = 0;
-    CC1D_TRY(occupancy(pl.k, pl.max_smem, dev, &occ));
-    GenericParams g{};
-    g.x = x, g.weight = weight, g.bias = bias, g.init = initial_states, g.seq = seq_idx;
-    g.dy = dout, g.dfinal = dfinal_states, g.dx = dx, g.dinit = dinit, g.partials = partials, g.status = di.status;
-    g.sxb = stride_x_batch, g.sxt = stride_x_time, g.syb = stride_dout_batch, g.syt = stride_dout_time;
-    g.B = static_cast<int>(B), g.T = static_cast<int>(T), g.D = static_cast<int>(D), g.W = static_cast<int>(W);
-    g.n_tt = pl.n_tt, g.n_dc = pl.n_blk;
-    g.w_dtype = weight_dtype, g.b_dtype = bias_dtype, g.init_dtype = init_dtype, g.silu = silu != 0;
-    void* args[] = {&g};
-    CC1D_TRY_CUDA(
-        cudaLaunchKernel(pl.k.fn, dim3(static_cast<unsigned>(pl.grid)), dim3(pl.k.threads), args, pl.k.smem, stream));
-  }
-
-  // Second stage: fixed-order sum over the P partial rows (32 column groups x 32 row slices per block).
-  const int64_t N = (W + 1) * D;
-  const bool vec4 = N % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0;
-  const int64_t groups = vec4 ? N / 4 : N;
-  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(cdiv(groups, kReduceCols), 65535)));
-  const int rthreads = kReduceCols * kReduceSlices;
-  if (vec4)
-    cc1d_reduce_partials_kernel<4><<<blocks, rthreads, 0, stream>>>(partials, pl.P, static_cast<int>(D),
-                                                                    static_cast<int>(W), dweight, weight_dtype,
-                                                                    bias ? dbias : nullptr, bias_dtype, grad_f32,
-                                                                    bias != nullptr);
-  else
-    cc1d_reduce_partials_kernel<1><<<blocks, rthreads, 0, stream>>>(partials, pl.P, static_cast<int>(D),
-                                                                    static_cast<int>(W), dweight, weight_dtype,
-                                                                    bias ? dbias : nullptr, bias_dtype, grad_f32,
-                                                                    bias != nullptr);
-  CC1D_TRY_CUDA(cudaGetLastError());
-  return CC1D_OK;
+  if (sum != dim) return CC1D_ERR_INVALID;
+  return bwd_impl(x, stride_x_batch, stride_x_time, weight, bias, initial_states, seq_idx, dout_pieces, n_pieces,
+                  dfinal_states, dx, stride_dx_batch, stride_dx_time, dweight, dbias, dinit, grad_f32, workspace,
+                  workspace_bytes, batch, seqlen, dim, width, x_dtype, weight_dtype, bias_dtype, init_dtype, silu,
+                  stream_, true);
 }
 
 }  // extern "C"

@@ -35,6 +35,9 @@
 
 namespace cc1d {
 
+// Most channel pieces dout may be split into (cc1d_bwd_split).
+constexpr int kMaxDoutPieces = 4;
+
 // Per-lane vector width and consumer warps per CTA. With SiLU the kernel is bound by arithmetic
 // latency and runs best with 8-byte lanes (4 channels of bf16) and 4 warps per CTA; without it the
 // kernel is bandwidth-bound and 4-byte lanes with 8 warps per CTA keep more rows in flight (both
@@ -67,15 +70,21 @@ struct BwdCfg {
 
 struct alignas(64) BwdWalkParams {
   CUtensorMap tmap_x;   // x as (D, T, B), box (D_TILE, RS + PAD, 1)
-  CUtensorMap tmap_dy;  // dout as (D, T, B), box (D_TILE, RS, 1)
+  // dout as up to kMaxDoutPieces channel ranges, each its own (channels, T, B) tensor map with box
+  // (D_TILE, RS, 1); piece i holds channels [dy_end[i-1], dy_end[i]) (dy_end[-1] = 0), and every
+  // piece boundary is a multiple of D_TILE, so each channel block reads from one piece.
+  CUtensorMap tmap_dy[kMaxDoutPieces];
   const void* weight;
   const void* bias;
   const void* init;     // (B, W-1, D) contiguous or null
   const int32_t* seq;   // (B, T) or null (the SEQ variant only)
   const void* dfinal;   // (B, W-1, D) contiguous, dtype of x, or null
-  void* dx;             // (B, T, D) contiguous
+  void* dx;             // (B, T, D) at strides (sdxb, sdxt, 1)
   void* dinit;          // (B, W-1, D) contiguous, dtype of init, or null
   float* partials;      // (P, W+1, D) fp32, P = gridDim.x / n_groups
+  int64_t sdxb, sdxt;   // dx strides in elements (channel stride 1)
+  int dy_end[kMaxDoutPieces];
+  int n_dy;
   unsigned* status;
   int64_t rows_per_part;  // L, a multiple of RS
   int B, T, D;
@@ -150,7 +159,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
     // ---------------- producer warp ----------------
     if (lane == 0) {
       prefetch_tensormap(&p.tmap_x);
-      prefetch_tensormap(&p.tmap_dy);
+      for (int i = 0; i < p.n_dy; ++i) prefetch_tensormap(&p.tmap_dy[i]);
     }
     int i = 0;
     bool ok = true;
@@ -168,7 +177,10 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
           for (int k = 0; k < nvb; ++k) {
             const int c0 = (g * C::WARPS + k) * DT;
             tma_load_3d(st + k * C::XROWS * C::ROW_BYTES, &p.tmap_x, &full[s], c0, a_lo - PAD, b);
-            tma_load_3d(st + C::XBYTES + k * RS * C::ROW_BYTES, &p.tmap_dy, &full[s], c0, a_lo, b);
+            int pc = 0;
+            while (pc + 1 < p.n_dy && c0 >= p.dy_end[pc]) ++pc;
+            tma_load_3d(st + C::XBYTES + k * RS * C::ROW_BYTES, &p.tmap_dy[pc], &full[s],
+                        c0 - (pc > 0 ? p.dy_end[pc - 1] : 0), a_lo, b);
           }
         }
         if constexpr (SEQ) {
@@ -327,7 +339,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
               for (int i2 = 0; i2 < NP; ++i2) gx[i2] = fadd2(gx[i2], v[i2]);
             }
           }
-          if (!GEN || dvalid) store_vec<T, CPT>(static_cast<T*>(p.dx) + (static_cast<int64_t>(b) * T_ + t) * D + d, gx);
+          if (!GEN || dvalid) store_vec<T, CPT>(static_cast<T*>(p.dx) + b * p.sdxb + t * p.sdxt + d, gx);
           // dweight / dbias partial sums (causal_conv1d.py:313-321).
 #pragma unroll
           for (int k = 0; k < PAD; ++k) {

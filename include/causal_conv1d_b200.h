@@ -42,7 +42,8 @@ enum {
   CC1D_ERR_UNSUPPORTED = 2, /* width above the largest supported (256) */
   CC1D_ERR_WORKSPACE = 3,   /* workspace smaller than cc1d_bwd_workspace_bytes() */
   CC1D_ERR_CUDA = 4,        /* a CUDA runtime/driver call failed; see cc1d_last_cuda_error() */
-  CC1D_ERR_SCRATCH_LIMIT = 5 /* cc1d_bwd_noalloc: problem needs more than its fixed scratch */
+  CC1D_ERR_SCRATCH_LIMIT = 5, /* cc1d_bwd_noalloc: problem needs more than its fixed scratch */
+  CC1D_ERR_LAYOUT = 6         /* cc1d_bwd_split: pieces or dx strides outside its fast path */
 };
 
 /* Interface version of this header; bumped on any signature change. */
@@ -146,6 +147,53 @@ int cc1d_bwd_noalloc(const void* x, int64_t stride_x_batch, int64_t stride_x_tim
                      void* dweight, void* dbias, void* dinit, float* grad_f32, int64_t batch,
                      int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype,
                      int bias_dtype, int init_dtype, int silu, void* stream);
+
+/* One channel range of dout held in its own tensor (cc1d_bwd_split). Element (b, t, c) of the
+ * piece, c in [0, channels), is at ptr + b*stride_batch + t*stride_time + c elements. */
+typedef struct cc1d_dout_piece {
+  const void* ptr;
+  int64_t stride_batch;
+  int64_t stride_time;
+  int64_t channels;
+} cc1d_dout_piece;
+
+enum { CC1D_MAX_DOUT_PIECES = 4 };
+
+/*
+ * Backward with dout given as channel pieces and dx written through strides: the layout of a
+ * Mamba-2 block, where the conv input xBC is a channel slice of the in_proj output zxbcdt and the
+ * conv output is split into the SSM's x, B and C. The gradients of x, B and C arrive as separate
+ * tensors; here they are read in place (no concatenation into one dout), and dx is written straight
+ * into the xBC slice of the caller's d(zxbcdt) buffer (no second concatenation). No counterpart in
+ * the reference, which takes one dout and returns a fresh dx (causal_conv1d.py:475-541).
+ *   dout_pieces     n_pieces (1..CC1D_MAX_DOUT_PIECES) pieces, covering channels [0, dim) in order;
+ *                   every piece boundary a multiple of 128 channels (64 for fp32)
+ *   dx              (B, T, D) at strides (stride_dx_batch, stride_dx_time, 1)
+ * Everything else as cc1d_bwd; size the workspace with cc1d_bwd_workspace_bytes() given the first
+ * piece as dout. The call needs the TMA path: widths 2..8; x, every piece and dx 16-byte aligned
+ * with 16-byte-multiple batch/time strides. Otherwise it returns CC1D_ERR_LAYOUT before any device
+ * work, and the caller concatenates dout and calls cc1d_bwd. Graph-capturable like cc1d_bwd.
+ */
+int cc1d_bwd_split(const void* x, int64_t stride_x_batch, int64_t stride_x_time,
+                   const void* weight, const void* bias, const void* initial_states,
+                   const int32_t* seq_idx, const cc1d_dout_piece* dout_pieces, int n_pieces,
+                   const void* dfinal_states, void* dx, int64_t stride_dx_batch,
+                   int64_t stride_dx_time, void* dweight, void* dbias, void* dinit,
+                   float* grad_f32, void* workspace, int64_t workspace_bytes, int64_t batch,
+                   int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype,
+                   int bias_dtype, int init_dtype, int silu, void* stream);
+
+/*
+ * Copies a (batch, seqlen, channels) block of elem_bytes-sized elements from src to dst, each at its
+ * own batch/time strides (in elements; channel stride 1). The glue around cc1d_bwd_split: it places
+ * dz and ddt in d(zxbcdt) at full bandwidth (16-byte vectors when the addresses and strides allow),
+ * where an element-wise copy into a strided slice runs at a fraction of it. No counterpart in the
+ * reference. Graph-capturable; allocates nothing.
+ */
+int cc1d_copy_channels(void* dst, int64_t dst_stride_batch, int64_t dst_stride_time,
+                       const void* src, int64_t src_stride_batch, int64_t src_stride_time,
+                       int64_t batch, int64_t seqlen, int64_t channels, int elem_bytes,
+                       void* stream);
 
 /*
  * Reads the device status word of the current device after synchronising it, and clears it when

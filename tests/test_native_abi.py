@@ -43,11 +43,28 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_and_error_strings():
     from causal_conv1d_b200 import _native
 
-    assert _native.lib.cc1d_abi_version() == 1
+    assert _native.lib.cc1d_abi_version() == 2
     assert _native.lib.cc1d_error_string(0) == b"success"
-    for code in (1, 2, 3, 4):
+    for code in (1, 2, 3, 4, 5, 6):
         assert len(_native.lib.cc1d_error_string(code)) > 5
     assert _native.lib.cc1d_error_string(99) == b"unknown error"
+
+
+def test_split_backward_rejects_bad_pieces_without_device_work():
+    """cc1d_bwd_split validates its pieces (count, widths, coverage of dim) before any CUDA call."""
+    from causal_conv1d_b200 import _native
+
+    lib, P = _native.lib, _native.DoutPiece
+
+    def call(pieces, dim=256):
+        arr = (P * max(1, len(pieces)))(*pieces)
+        return lib.cc1d_bwd_split(None, 0, 0, None, None, None, None, arr, len(pieces), None, None, 0, 0,
+                                  None, None, None, None, None, 0, 2, 8, dim, 4, 2, 0, 0, 0, 1, None)
+
+    assert call([]) == _native.CC1D_ERR_INVALID
+    assert call([P(None, 0, 0, 128)] * 5, dim=640) == _native.CC1D_ERR_INVALID  # above the limit
+    assert call([P(None, 0, 0, 128), P(None, 0, 0, 0), P(None, 0, 0, 128)]) == _native.CC1D_ERR_INVALID
+    assert call([P(None, 0, 0, 128), P(None, 0, 0, 64)]) == _native.CC1D_ERR_INVALID  # 192 != 256
 
 
 def test_invalid_sizes_rejected_without_device_work():
