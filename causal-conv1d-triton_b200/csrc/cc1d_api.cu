@@ -148,6 +148,15 @@ bool encode_3d(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t
   return r == CUDA_SUCCESS;
 }
 
+// Template width of the TMA kernels for a true width W, or 0 for the generic path. Widths 9..16
+// run on the width-12 or width-16 kernels with leading zero taps (identical results).
+int tma_width(int64_t W) {
+  if (W <= 8) return static_cast<int>(W);
+  if (W <= 12) return 12;
+  if (W <= 16) return 16;
+  return 0;
+}
+
 KernelInfo fwd_tma_for(int dtype, int W, bool seq, bool silu) {
   if (dtype == kBF16) return fwd_tma_info<__nv_bfloat16>(W, seq, silu);
   if (dtype == kF16) return fwd_tma_info<__half>(W, seq, silu);
@@ -188,6 +197,7 @@ int check_sizes(int64_t B, int64_t T, int64_t D, int64_t W) {
 // Launch plan of the backward: which kernel, how many CTAs, how many partial rows.
 struct BwdPlan {
   bool tma = false;
+  int wt = 0;     // template width of the TMA kernels (0: generic path)
   KernelInfo k;
   int max_smem = 0;
   int P = 0;      // partial rows (CTAs per channel block / group)
@@ -201,17 +211,18 @@ struct BwdPlan {
 int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t syb, int64_t syt, int64_t B, int64_t T,
              int64_t D, int64_t W, int x_dtype, bool seq, bool silu, const DeviceInfo& di, int dev, BwdPlan* pl) {
   const int es = elem_size(x_dtype);
-  pl->tma = W <= 8 && tma_layout_ok(x, sxb, sxt, B, D, es) && tma_layout_ok(dy, syb, syt, B, D, es);
+  pl->wt = tma_width(W);
+  pl->tma = pl->wt > 0 && tma_layout_ok(x, sxb, sxt, B, D, es) && tma_layout_ok(dy, syb, syt, B, D, es);
   int occ = 0;
   if (pl->tma) {
-    pl->k = bwd_tma_for(x_dtype, static_cast<int>(W), seq, silu);
+    pl->k = bwd_tma_for(x_dtype, pl->wt, seq, silu);
     pl->max_smem = pl->k.smem;
     // The partial count must not depend on seq_idx or the activation (the workspace query sees
     // neither): size the grid by the lowest occupancy of the four variants, all of which cover the
     // same channels per CTA.
     occ = 1 << 30;
     for (int v = 0; v < 4; ++v) {
-      const KernelInfo kv = bwd_tma_for(x_dtype, static_cast<int>(W), (v & 1) != 0, (v & 2) != 0);
+      const KernelInfo kv = bwd_tma_for(x_dtype, pl->wt, (v & 1) != 0, (v & 2) != 0);
       if (kv.d_tile != pl->k.d_tile) return CC1D_ERR_INVALID;
       int o = 0;
       CC1D_TRY(occupancy(kv, kv.smem, dev, &o));
@@ -328,7 +339,7 @@ int bwd_impl(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
   bool launched = false;
   if (pl.tma) {
     BwdWalkParams p{};
-    const int PADi = static_cast<int>(PAD);
+    const int PADi = pl.wt - 1;  // halo rows of the template width
     const int box_d = pl.k.box_d;  // one channel block per consumer warp
     bool maps = encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, box_d, pl.k.t_tile + PADi);
     int64_t c_end = 0;
@@ -347,7 +358,7 @@ int bwd_impl(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
       p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
       p.dfinal = dfinal_states, p.dx = dx, p.dinit = dinit, p.partials = partials, p.status = di.status;
       p.rows_per_part = pl.rows_per_part;
-      p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D);
+      p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D), p.W = static_cast<int>(W);
       p.n_groups = pl.n_blk;
       p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
       void* args[] = {&p};
@@ -469,17 +480,17 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
   if (!x || !weight || !out) return CC1D_ERR_INVALID;
 
   const int es = elem_size(x_dtype);
-  if (W <= 8 && tma_layout_ok(x, stride_x_batch, stride_x_time, B, D, es)) {
-    const KernelInfo k = fwd_tma_for(x_dtype, static_cast<int>(W), seq_idx != nullptr, silu != 0);
+  const int wt = tma_width(W);
+  if (wt > 0 && tma_layout_ok(x, stride_x_batch, stride_x_time, B, D, es)) {
+    const KernelInfo k = fwd_tma_for(x_dtype, wt, seq_idx != nullptr, silu != 0);
     FwdParams p{};
-    if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, k.d_tile,
-                  k.t_tile + static_cast<int>(PAD))) {
+    if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, k.d_tile, k.t_tile + wt - 1)) {
       int occ = 0;
       CC1D_TRY(occupancy(k, k.smem, dev, &occ));
       p.x = x, p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
       p.out = out, p.final_states = final_states, p.status = di.status;
       p.sxb = stride_x_batch, p.sxt = stride_x_time;
-      p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D);
+      p.B = static_cast<int>(B), p.T = static_cast<int>(T), p.D = static_cast<int>(D), p.W = static_cast<int>(W);
       p.n_tt = static_cast<int>(cdiv(T, k.t_tile));
       p.n_db = static_cast<int>(cdiv(D, k.d_tile));
       p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;

@@ -45,12 +45,14 @@ constexpr int kMaxDoutPieces = 4;
 template <typename T, int W, bool SILU>
 struct BwdCfg {
   static constexpr int ES = static_cast<int>(sizeof(T));
-  static constexpr int VEC = (SILU || W > 4 || ES == 4) ? 8 : 4;  // bytes per lane
+  // bytes per lane: 8 with SiLU, above W = 4 and for fp32; 4 without SiLU up to W = 4 and for
+  // 16-bit template widths above 8 (whose 4-channel taps, sums and windows would not fit).
+  static constexpr int VEC = ES == 4 ? 8 : (W > 8 ? 4 : ((SILU || W > 4) ? 8 : 4));
   static constexpr int ROW_BYTES = 32 * VEC;     // one channel block's row segment
   static constexpr int D_TILE = ROW_BYTES / ES;  // channels per warp
   static constexpr int CPT = VEC / ES;           // channels per lane
   static constexpr int NP = CPT / 2;             // fp32 pairs per lane
-  static constexpr int WARPS = VEC == 8 ? 4 : 8; // consumer warps = channel blocks per CTA
+  static constexpr int WARPS = (VEC == 8 || W > 8) ? 4 : 8;  // consumer warps = channel blocks per CTA
   static constexpr int THREADS = WARPS * 32 + 32;
   static constexpr int DG = WARPS * D_TILE;      // channels per CTA
   static constexpr int RS = 16;                  // rows per stage
@@ -88,6 +90,7 @@ struct alignas(64) BwdWalkParams {
   unsigned* status;
   int64_t rows_per_part;  // L, a multiple of RS
   int B, T, D;
+  int W;                  // true width: the template width less any leading zero taps
   int n_groups;           // channel groups of DG channels
   int w_dtype, b_dtype, init_dtype;
 };
@@ -209,8 +212,13 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
   // at the end (all exact power-of-two scalings).
   constexpr bool HALF = SILU && FAST;
   float2 w[W][NP], bv[NP];
-  load_taps<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, w, bv);
+  if (p.W == W) {
+    load_taps<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, w, bv);
+  } else {
+    load_taps_off<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, p.W, w, bv);
+  }
   if constexpr (HALF) halve_taps<W, NP>(w, bv);
+  const int pw = p.W - 1, off = W - p.W;  // true state rows; leading zero taps
   float2 dw[W][NP], dbs[NP];
 #pragma unroll
   for (int i2 = 0; i2 < NP; ++i2) {
@@ -258,8 +266,9 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
           constexpr bool GEN = decltype(general)::value;
           const int q = RS - 1 + PAD - ix;
           if (GEN && has_init && a_lo - PAD + q < 0) {
-            if (dvalid) {
-              load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * PAD + (a_lo + q), p.D, d, xr[ix]);
+            const int ir = a_lo - PAD + q + pw;  // initial_states row of t = a_lo - PAD + q
+            if (dvalid && ir >= 0) {
+              load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * pw + ir, p.D, d, xr[ix]);
             } else {
 #pragma unroll
               for (int i2 = 0; i2 < NP; ++i2) xr[ix][i2] = make_float2(0.f, 0.f);
@@ -331,10 +340,10 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
             }
           }
           if (GEN && p.dfinal != nullptr && dvalid) {
-            const int f = t - (T_ - PAD);
+            const int f = t - (T_ - pw);
             if (f >= 0) {
               float2 v[NP];
-              load_state_row<NP>(p.dfinal, XDT, static_cast<int64_t>(b) * PAD + f, p.D, d, v);
+              load_state_row<NP>(p.dfinal, XDT, static_cast<int64_t>(b) * pw + f, p.D, d, v);
 #pragma unroll
               for (int i2 = 0; i2 < NP; ++i2) gx[i2] = fadd2(gx[i2], v[i2]);
             }
@@ -376,6 +385,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
           const int seq0 = SEQ ? sq[PAD - 1] : 0;  // rows t < 0 carry seq_idx[b, 0]
 #pragma unroll
           for (int q = 1; q <= PAD; ++q) {
+            if (q > pw) break;  // rows t < -(W-1) have no initial state (their taps are zero)
             const int t = -q;
             float2 gx[NP];
 #pragma unroll
@@ -388,15 +398,15 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
               }
             }
             if (p.dfinal != nullptr) {
-              const int f = t - (T_ - PAD);
+              const int f = t - (T_ - pw);
               if (f >= 0) {
                 float2 v[NP];
-                load_state_row<NP>(p.dfinal, XDT, static_cast<int64_t>(b) * PAD + f, p.D, d, v);
+                load_state_row<NP>(p.dfinal, XDT, static_cast<int64_t>(b) * pw + f, p.D, d, v);
 #pragma unroll
                 for (int i2 = 0; i2 < NP; ++i2) gx[i2] = fadd2(gx[i2], v[i2]);
               }
             }
-            const int64_t o = (static_cast<int64_t>(b) * PAD + t + PAD) * D + d;
+            const int64_t o = (static_cast<int64_t>(b) * pw + t + pw) * D + d;
 #pragma unroll
             for (int i2 = 0; i2 < NP; ++i2) {
               st_any(p.dinit, o + 2 * i2, p.init_dtype, gx[i2].x);
@@ -421,13 +431,16 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
   }
   // This thread's channels belong to this warp alone: write the partial sums directly.
   if (dvalid) {
-    float* pp = p.partials + static_cast<int64_t>(part) * (W + 1) * D + d;
+    // Partial row layout (W+1, D) with the true width; the leading zero taps are not stored.
+    float* pp = p.partials + static_cast<int64_t>(part) * (p.W + 1) * D + d;
 #pragma unroll
-    for (int k = 0; k < W; ++k)
+    for (int k = 0; k < W; ++k) {
+      if (k < off) continue;
 #pragma unroll
-      for (int i2 = 0; i2 < NP; ++i2) *reinterpret_cast<float2*>(pp + k * D + 2 * i2) = dw[k][i2];
+      for (int i2 = 0; i2 < NP; ++i2) *reinterpret_cast<float2*>(pp + (k - off) * D + 2 * i2) = dw[k][i2];
+    }
 #pragma unroll
-    for (int i2 = 0; i2 < NP; ++i2) *reinterpret_cast<float2*>(pp + W * D + 2 * i2) = dbs[i2];
+    for (int i2 = 0; i2 < NP; ++i2) *reinterpret_cast<float2*>(pp + p.W * D + 2 * i2) = dbs[i2];
   }
 }
 

@@ -44,6 +44,8 @@ KernelInfo fwd_tma_info(int W, bool seq, bool silu) {
     case 6: return detail::fwd_tma_w<T, 6>(seq, silu);
     case 7: return detail::fwd_tma_w<T, 7>(seq, silu);
     case 8: return detail::fwd_tma_w<T, 8>(seq, silu);
+    case 12: return detail::fwd_tma_w<T, 12>(seq, silu);
+    case 16: return detail::fwd_tma_w<T, 16>(seq, silu);
     default: return {};
   }
 }
@@ -58,6 +60,8 @@ KernelInfo bwd_tma_info(int W, bool seq, bool silu) {
     case 6: return detail::bwd_tma_w<T, 6>(seq, silu);
     case 7: return detail::bwd_tma_w<T, 7>(seq, silu);
     case 8: return detail::bwd_tma_w<T, 8>(seq, silu);
+    case 12: return detail::bwd_tma_w<T, 12>(seq, silu);
+    case 16: return detail::bwd_tma_w<T, 16>(seq, silu);
     default: return {};
   }
 }

@@ -47,7 +47,7 @@ struct TileCfg {
   static constexpr int R = T_TILE / RG;               // rows per thread per tile: 16 or 32
   static constexpr int PAD = W - 1;
   static_assert(LANES_D % 32 == 0 && RG * LANES_D == CONSUMERS, "row groups are whole warps");
-  static_assert(W >= 2 && W <= 8, "TMA path covers widths 2..8");
+  static_assert(W >= 2 && W <= 16, "TMA path covers template widths 2..16");
   static_assert(R >= PAD, "only row group 0 of the first tile reads rows t < 0");
 };
 
@@ -61,8 +61,9 @@ struct FwdLayout {
   static constexpr int XBYTES = XROWS * C::ROW_BYTES;
   static constexpr int SEQ_BYTES = SEQ ? (XROWS * 4 + 127) / 128 * 128 : 0;
   // Registers are bounded for 6 CTAs (24 warps) per SM with 8-byte vectors, 8 CTAs with 4-byte
-  // vectors; 17-18 KB of shared memory each.
-  static constexpr int MIN_CTAS = C::VEC_BYTES == 4 ? 8 : 6;
+  // vectors; 17-19 KB of shared memory each.
+  // Template widths 12 and 16 (taps and window of 2 x W fp32 values per channel pair) get 5.
+  static constexpr int MIN_CTAS = W > 8 ? 5 : (C::VEC_BYTES == 4 ? 8 : 6);
   static constexpr int SMEM_BYTES = kSmemAlign + kBarBytes + XBYTES + SEQ_BYTES;
 };
 
@@ -78,6 +79,7 @@ struct alignas(64) FwdParams {
   unsigned* status;
   int64_t sxb, sxt;    // x strides in elements (channel stride 1)
   int B, T, D;
+  int W;               // true width: the template width less any leading zero taps
   int n_tt, n_db;      // time tiles per row, channel blocks
   int w_dtype, b_dtype, init_dtype;
 };
@@ -169,6 +171,28 @@ __device__ __forceinline__ void halve_taps(float2 (&w)[W][NP], float2 (&bv)[NP])
   }
 }
 
+// load_taps for a true width Wt below the template width W: the (D, Wt) weight rows fill taps
+// W-Wt .. W-1 and the leading W-Wt taps are zero. A causal conv of width Wt equals the width-W conv
+// with those zero taps bit for bit on finite inputs (each zero product adds an exact zero).
+template <int W, int NP>
+__device__ __forceinline__ void load_taps_off(const void* weight, int w_dtype, const void* bias, int b_dtype, int d,
+                                              bool dvalid, int Wt, float2 (&w)[W][NP], float2 (&bv)[NP]) {
+  const int off = W - Wt;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const int64_t d0 = d + 2 * i;
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+      const int kk = k - off;
+      w[k][i] = (dvalid && kk >= 0)
+                    ? make_float2(ld_any(weight, d0 * Wt + kk, w_dtype), ld_any(weight, (d0 + 1) * Wt + kk, w_dtype))
+                    : make_float2(0.f, 0.f);
+    }
+    bv[i] = (dvalid && bias) ? make_float2(ld_any(bias, d0, b_dtype), ld_any(bias, d0 + 1, b_dtype))
+                             : make_float2(0.f, 0.f);
+  }
+}
+
 // Loads CPT channels of a row of a contiguous (B, W-1, D) state tensor (run-time dtype).
 template <int NP>
 __device__ __forceinline__ void load_state_row(const void* base, int dtype, int64_t row, int D, int d,
@@ -227,8 +251,13 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   const bool dvalid = d < p.D;  // D is a multiple of CPT on this path
   const int64_t D = p.D;
   float2 w[W][NP], bv[NP];
-  load_taps_fast<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, w, bv);
+  if (p.W == W) {
+    load_taps_fast<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, w, bv);
+  } else {
+    load_taps_off<W, NP>(p.weight, p.w_dtype, p.bias, p.b_dtype, d, dvalid, p.W, w, bv);
+  }
   if constexpr (SILU && FAST) halve_taps<W, NP>(w, bv);  // z below is h = z / 2
+  const int pw = p.W - 1, off = W - p.W;  // true state rows; leading zero taps
   __syncthreads();  // barrier initialised, seq window written
   if (!mbar_wait(full, 0, p.status)) return;
 
@@ -242,9 +271,9 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   float2 xw[NW][NP];
   if (p.init != nullptr && ts == 0) {
 #pragma unroll
-    for (int k = 0; k < PAD; ++k) {
-      if (dvalid) {
-        load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * PAD + k, p.D, d, xw[k]);
+    for (int k = 0; k < PAD; ++k) {  // row t = k - PAD is initial_states row k - off
+      if (dvalid && k >= off) {
+        load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * pw + (k - off), p.D, d, xw[k]);
       } else {
 #pragma unroll
         for (int i2 = 0; i2 < NP; ++i2) xw[k][i2] = make_float2(0.f, 0.f);
@@ -286,21 +315,22 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
     if (full_rows || (dvalid && ts + r < p.T)) store_vec<T, CPT>(orow + r * D, z);
   });
 
-  // final_states = last PAD rows of concat(initial_states, x) (causal_conv1d.py:153-164).
+  // final_states = last W-1 rows (true width) of concat(initial_states, x) (causal_conv1d.py:153-164).
   if (p.final_states != nullptr && tt == p.n_tt - 1 && rg == 0 && dvalid) {
 #pragma unroll
     for (int q = 0; q < PAD; ++q) {
-      const int src = p.T - PAD + q;
+      if (q >= pw) break;
+      const int src = p.T - pw + q;
       float2 v[NP];
       if (src >= 0) {
         load_vec<T, CPT>(static_cast<const T*>(p.x) + b * p.sxb + src * p.sxt + d, v);
       } else if (p.init != nullptr) {
-        load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * PAD + src + PAD, p.D, d, v);
+        load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * pw + src + pw, p.D, d, v);
       } else {
 #pragma unroll
         for (int i2 = 0; i2 < NP; ++i2) v[i2] = make_float2(0.f, 0.f);
       }
-      store_vec<T, CPT>(static_cast<T*>(p.final_states) + (static_cast<int64_t>(b) * PAD + q) * D + d, v);
+      store_vec<T, CPT>(static_cast<T*>(p.final_states) + (static_cast<int64_t>(b) * pw + q) * D + d, v);
     }
   }
 }
