@@ -90,15 +90,48 @@ __global__ void __launch_bounds__(GTHREADS) cc1d_fwd_generic_kernel(const Generi
     for (int r = tid; r < GT + PAD; r += GTHREADS) sq[r] = seq_generic(p, b, t0 - PAD + r);
   __syncthreads();
 
-  const int c = tid % GC, rl = tid / GC, d = d0 + c;
+  // Thread (row group rg, channel c) computes the GRB = 8 consecutive rows r0 .. r0 + 7 of its
+  // channel, taps outer: one shared-memory load of a tap and one of a new input row feed 8 FMAs.
+  // acc[j] takes z = w[PAD] x[t] then taps k = 0..PAD-1 in order, the reference's order per element.
+  // The 8-row input window is a ring indexed by compile-time slots (tap loop unrolled by 8).
+  constexpr int GRB = GT / (GTHREADS / GC);
+  static_assert(GRB == 8, "8 rows per thread");
+  const int c = tid % GC, r0 = (tid / GC) * GRB, d = d0 + c;
   const float bias = (p.bias != nullptr && d < p.D) ? ld_any(p.bias, d, p.b_dtype) : 0.0f;
-  for (int r = rl; r < GT && t0 + r < p.T; r += GTHREADS / GC) {
-    const int seq_t = p.seq ? sq[r + PAD] : 0;
-    float z = ws[PAD * GC + c] * xs[(r + PAD) * GC + c];
-    for (int k = 0; k < PAD; ++k)
-      if (!p.seq || sq[r + k] == seq_t) z = fmaf(ws[k * GC + c], xs[(r + k) * GC + c], z);
-    z += bias;
-    if (p.seq && seq_t < 0) z = 0.0f;
+  const bool seq = p.seq != nullptr;
+  float acc[GRB], xr[GRB];
+  int st[GRB], sr[GRB];  // seq id of each output row; ring of the input rows' seq ids
+  const float wl = ws[PAD * GC + c];
+#pragma unroll
+  for (int j = 0; j < GRB; ++j) {
+    acc[j] = wl * xs[(r0 + j + PAD) * GC + c];
+    xr[j] = xs[(r0 + j) * GC + c];  // window of tap 0: rows r0 .. r0 + 7 (local x rows)
+    st[j] = seq ? sq[r0 + j + PAD] : 0;
+    sr[j] = seq ? sq[r0 + j] : 0;
+  }
+  for (int k0 = 0; k0 < PAD; k0 += GRB) {
+#pragma unroll
+    for (int kk = 0; kk < GRB; ++kk) {
+      const int k = k0 + kk;
+      if (k < PAD) {
+        const float wk = ws[k * GC + c];
+#pragma unroll
+        for (int j = 0; j < GRB; ++j)
+          if (!seq || sr[(j + kk) % GRB] == st[j]) acc[j] = fmaf(wk, xr[(j + kk) % GRB], acc[j]);
+        // Slide: slot kk held row r0 + k; it takes row r0 + k + 8 (read up to row GT + PAD - 1).
+        if (k + GRB < GT + PAD - r0) {
+          xr[kk] = xs[(r0 + k + GRB) * GC + c];
+          if (seq) sr[kk] = sq[r0 + k + GRB];
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < GRB; ++j) {
+    const int r = r0 + j;
+    if (t0 + r >= p.T) break;
+    float z = acc[j] + bias;
+    if (seq && st[j] < 0) z = 0.0f;
     if (p.silu) z = silu_generic(z, FAST);
     if (d < p.D) static_cast<T*>(p.out)[(static_cast<int64_t>(b) * p.T + t0 + r) * p.D + d] = from_f<T>(z);
   }
