@@ -105,3 +105,32 @@ def test_api_errors_match_reference():
         causal_conv1d_fn(x, torch.randn(4, 1))
     with pytest.raises(AssertionError):  # x must be on a CUDA device
         causal_conv1d_fn(x, w)
+
+
+def test_split_conv1d_argument_errors():
+    """split_conv1d checks its arguments on the host before any device work."""
+    from causal_conv1d_b200 import split_conv1d
+
+    zx = torch.randn(2, 8, 20)
+    w = torch.randn(12, 4)
+    with pytest.raises(NotImplementedError):
+        split_conv1d(zx, w, d_z=4, xbc_split=(8, 2, 2), activation="gelu")
+    with pytest.raises(AssertionError):  # zxbcdt must be 3-D
+        split_conv1d(zx[0], w, d_z=4, xbc_split=(8, 2, 2))
+    with pytest.raises(AssertionError):  # z + xBC wider than zxbcdt
+        split_conv1d(zx, w, d_z=10, xbc_split=(8, 2, 2))
+    with pytest.raises(AssertionError):  # empty piece
+        split_conv1d(zx, w, d_z=4, xbc_split=(12, 0))
+    with pytest.raises(AssertionError):  # weight rows must equal sum(xbc_split)
+        split_conv1d(zx, torch.randn(10, 4), d_z=4, xbc_split=(8, 2, 2))
+    with pytest.raises(AssertionError):  # zxbcdt must be on a CUDA device
+        split_conv1d(zx, w, d_z=4, xbc_split=(8, 2, 2))
+
+
+def test_copy_channels_rejects_bad_arguments():
+    from causal_conv1d_b200 import _native
+
+    lib = _native.lib
+    assert lib.cc1d_copy_channels(None, 0, 0, None, 0, 0, 1, 1, 1, 3, None) == _native.CC1D_ERR_INVALID
+    assert lib.cc1d_copy_channels(None, 0, 0, None, 0, 0, -1, 1, 1, 2, None) == _native.CC1D_ERR_INVALID
+    assert lib.cc1d_copy_channels(None, 0, 0, None, 0, 0, 0, 8, 8, 2, None) == _native.CC1D_OK  # empty
