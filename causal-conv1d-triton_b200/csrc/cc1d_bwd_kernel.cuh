@@ -1,4 +1,4 @@
-// TMA-pipelined sm_100a backward of the causal depthwise conv1d (widths 2..8):
+// TMA-pipelined sm_100a backward of the causal depthwise conv1d (template widths 2..8, 12, 16):
 //
 //   dz[t]  = dout[t] * act'(z[t]),   z[t] = bias + sum_k w[k] x[t-(W-1)+k]    (recomputed)
 //   dx[t]  = sum_{j=0..W-1} w[W-1-j] dz[t+j]                                  (+ dfinal_states)

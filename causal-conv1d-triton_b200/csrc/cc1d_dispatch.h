@@ -17,7 +17,7 @@ struct KernelInfo {
   bool persistent = true;    // grid sized to the resident CTAs (false: one CTA per tile)
 };
 
-// TMA path, widths 2..8; fn is null for widths outside that range.
+// TMA path, template widths 2..8, 12 and 16; fn is null for other widths.
 template <typename T> KernelInfo fwd_tma_info(int W, bool seq, bool silu);
 template <typename T> KernelInfo bwd_tma_info(int W, bool seq, bool silu);
 // Generic path, any width up to kGenericMaxWidth.

@@ -170,7 +170,7 @@ enum { CC1D_MAX_DOUT_PIECES = 4 };
  *                   every piece boundary a multiple of 128 channels (64 for fp32)
  *   dx              (B, T, D) at strides (stride_dx_batch, stride_dx_time, 1)
  * Everything else as cc1d_bwd; size the workspace with cc1d_bwd_workspace_bytes() given the first
- * piece as dout. The call needs the TMA path: widths 2..8; x, every piece and dx 16-byte aligned
+ * piece as dout. The call needs the TMA path: widths 2..16; x, every piece and dx 16-byte aligned
  * with 16-byte-multiple batch/time strides. Otherwise it returns CC1D_ERR_LAYOUT before any device
  * work, and the caller concatenates dout and calls cc1d_bwd. Graph-capturable like cc1d_bwd.
  */
