@@ -486,7 +486,7 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
     FwdParams p{};
     if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, k.d_tile, k.t_tile + wt - 1)) {
       int occ = 0;
-      CC1D_TRY(occupancy(k, k.smem, dev, &occ));
+      CC1D_TRY(occupancy(k, k.smem, dev, &occ));  // also raises the kernel's dynamic shared memory limit
       p.x = x, p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;
       p.out = out, p.final_states = final_states, p.status = di.status;
       p.sxb = stride_x_batch, p.sxt = stride_x_time;
@@ -494,10 +494,7 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
       p.n_tt = static_cast<int>(cdiv(T, k.t_tile));
       p.n_db = static_cast<int>(cdiv(D, k.d_tile));
       p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
-      const int64_t M = B * p.n_tt;
-      const int64_t cap = static_cast<int64_t>(di.sms) * occ;
-      const int64_t P = k.persistent ? std::max<int64_t>(1, std::min<int64_t>(M, cap / p.n_db)) : M;
-      const int64_t grid = P * p.n_db;
+      const int64_t grid = B * p.n_tt * p.n_db;  // one CTA per (batch row, time tile, channel block)
       if (grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
       void* args[] = {&p};
       CC1D_TRY_CUDA(cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(grid)), dim3(k.threads), args, k.smem, stream));

@@ -14,7 +14,6 @@ struct KernelInfo {
   int d_tile = 0;            // channels per CTA tile (per CTA channel group for the TMA backward)
   int t_tile = 0;            // time rows per CTA tile (per pipeline stage for the TMA backward)
   int box_d = 0;             // channels per TMA box (TMA backward: per consumer warp)
-  bool persistent = true;    // grid sized to the resident CTAs (false: one CTA per tile)
 };
 
 // TMA path, template widths 2..8, 12 and 16; fn is null for other widths.

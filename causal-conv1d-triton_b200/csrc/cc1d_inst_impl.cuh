@@ -10,10 +10,8 @@ namespace detail {
 template <typename T, int W, bool SEQ, bool SILU>
 KernelInfo fwd_tma_one() {
   using C = TileCfg<T, W>;
-  KernelInfo k{reinterpret_cast<const void*>(&cc1d_fwd_tma_kernel<T, W, SEQ, SILU>), FwdLayout<T, W, SEQ>::SMEM_BYTES,
-               C::CONSUMERS, C::D_TILE, C::T_TILE, C::D_TILE};
-  k.persistent = false;
-  return k;
+  return {reinterpret_cast<const void*>(&cc1d_fwd_tma_kernel<T, W, SEQ, SILU>), FwdLayout<T, W, SEQ>::SMEM_BYTES,
+          C::CONSUMERS, C::D_TILE, C::T_TILE, C::D_TILE};
 }
 template <typename T, int W, bool SEQ, bool SILU>
 KernelInfo bwd_tma_one() {
