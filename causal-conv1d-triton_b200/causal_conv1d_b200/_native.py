@@ -53,6 +53,7 @@ SIGNATURES = {
                         _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _I, _I, _I,
                         _I, _P], _I),
     "cc1d_copy_channels": ([_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I, _P], _I),
+    "cc1d_selftest_wait_timeout": ([_P], _I),
     "cc1d_status": ([ctypes.POINTER(ctypes.c_uint32), _I], _I),
     "cc1d_error_string": ([_I], ctypes.c_char_p),
     "cc1d_last_cuda_error": ([], _I),

@@ -447,6 +447,15 @@ const char* cc1d_error_string(int code) {
 
 int cc1d_last_cuda_error(void) { return t_last_cuda_error; }
 
+int cc1d_selftest_wait_timeout(void* stream_) {
+  DeviceInfo di;
+  int dev = 0;
+  CC1D_TRY(device_info(&di, &dev));
+  cc1d_wait_timeout_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream_)>>>(di.status);
+  CC1D_TRY_CUDA(cudaGetLastError());
+  return CC1D_OK;
+}
+
 int cc1d_status(uint32_t* status, int clear) {
   DeviceInfo di;
   int dev = 0;

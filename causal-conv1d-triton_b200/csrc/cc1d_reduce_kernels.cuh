@@ -77,6 +77,18 @@ __global__ void __launch_bounds__(kReduceCols * kReduceSlices)
   }
 }
 
+// Waits on a shared-memory mbarrier that nothing completes: the bounded wait gives up after
+// kWaitLimitNs and records kStatusWaitTimeout (the failure-detection self-test).
+__global__ void cc1d_wait_timeout_probe_kernel(unsigned* status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  mbar_wait(&bar, 0, status);  // phase 0 never completes: no thread arrives
+}
+
 // dst[i] = src[i] converted (or 0 when src is null), i < n.
 __global__ void cc1d_fill_kernel(void* dst, int dst_dtype, const void* src, int src_dtype, int64_t n) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;

@@ -202,6 +202,16 @@ int cc1d_copy_channels(void* dst, int64_t dst_stride_batch, int64_t dst_stride_t
  */
 int cc1d_status(uint32_t* status, int clear);
 
+/*
+ * Self-test of the failure detection: launches one block whose threads wait on a shared-memory
+ * mbarrier that nothing ever completes, with the same bounded wait as the kernels (about one
+ * second), so the wait gives up, sets bit 0 of the device status word and the kernel returns; no
+ * fault, and the context stays usable. cc1d_status() then reports the bit. No counterpart in the
+ * reference (its Triton kernels have no waits); it exists so that the timeout path can be checked
+ * on a real GPU.
+ */
+int cc1d_selftest_wait_timeout(void* stream);
+
 /* Human-readable text for a CC1D_ERR_* code. */
 const char* cc1d_error_string(int code);
 
