@@ -44,6 +44,21 @@ def _channels_contiguous(t: Tensor) -> Tensor:
     return t if t.stride(-1) == 1 else t.contiguous()
 
 
+def _tma_layout(t: Tensor, width: int) -> Tensor:
+    """`t` itself, or a fresh contiguous copy when its base or batch/time strides are not the
+    16-byte multiples the TMA kernels need while its rows are (channels x element size a multiple of
+    16 bytes) and the width is one those kernels cover (<= 16), e.g. a column slice at an odd
+    offset. The copy is one pass over t; the per-element generic kernels it avoids ran ~5x slower on
+    B200 (B=8 T=8192 D=1024 W=4 bf16, forward + backward). Differentiable (a clone)."""
+    B, T, D = t.shape
+    es = t.element_size()
+    if width > 16 or (D * es) % 16 != 0 or t.numel() == 0:
+        return t
+    aligned = (t.data_ptr() % 16 == 0 and (t.stride(1) * es) % 16 == 0
+               and (B == 1 or (t.stride(0) * es) % 16 == 0))
+    return t if aligned else t.clone(memory_format=torch.contiguous_format)
+
+
 def _as_float(t: Tensor | None) -> Tensor | None:
     """Parameters in a float type the kernels do not read (e.g. float64) are passed as fp32."""
     if t is None or t.dtype in _FLOAT:
@@ -255,9 +270,9 @@ class _CausalConv1dFn(torch.autograd.Function):
         if dfinal_states is not None:
             dfinal_states = dfinal_states.contiguous()
         need_dinit = initial_states is not None and ctx.needs_input_grad[4]
+        dout = _tma_layout(_channels_contiguous(dout), weight.shape[1])
         dx, dweight, dbias, dinit = _bwd(
-            x, weight, bias, seq_idx, initial_states, _channels_contiguous(dout), dfinal_states,
-            need_dinit, ctx.silu,
+            x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_dinit, ctx.silu,
         )
         return dx, dweight, dbias, None, dinit, None, None
 
@@ -296,7 +311,7 @@ def causal_conv1d_fn(
         assert return_final_states, "final_states_out requires return_final_states=True"
     _check_inputs(x, weight, bias, seq_idx, initial_states)
 
-    x = _channels_contiguous(x)
+    x = _tma_layout(_channels_contiguous(x), weight.shape[1])
     weight = weight.contiguous()
     bias = bias.contiguous() if bias is not None else None
     seq_idx = seq_idx.to(torch.int32).contiguous() if seq_idx is not None else None

@@ -24,23 +24,25 @@ from typing import Sequence
 import torch
 from torch import Tensor
 
-from .causal_conv1d import _bwd_split, _check_inputs, _copy_channels, _fwd
+from .causal_conv1d import _bwd_split, _check_inputs, _copy_channels, _fwd, _tma_layout
 
 
 class _SplitConv1dFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, zxbcdt, weight, bias, seq_idx, initial_states, d_z, xbc_split, silu):
         d_xbc = sum(xbc_split)
-        xbc = zxbcdt[..., d_z:d_z + d_xbc]
+        # A slice the TMA kernels cannot address is copied once, as causal_conv1d_fn does, and the
+        # copy serves the backward too.
+        xbc = _tma_layout(zxbcdt[..., d_z:d_z + d_xbc], weight.shape[1])
         out = _fwd(xbc, weight, bias, seq_idx, initial_states, None, silu)
-        ctx.save_for_backward(zxbcdt, weight, bias, seq_idx, initial_states)
+        ctx.save_for_backward(zxbcdt, weight, bias, seq_idx, initial_states, xbc)
         ctx.d_z, ctx.xbc_split, ctx.silu = d_z, xbc_split, silu
         parts = out.split(list(xbc_split), dim=-1)
         return (zxbcdt[..., :d_z], *parts, zxbcdt[..., d_z + d_xbc:])
 
     @staticmethod
     def backward(ctx, dz, *grads):
-        zxbcdt, weight, bias, seq_idx, initial_states = ctx.saved_tensors
+        zxbcdt, weight, bias, seq_idx, initial_states, xbc = ctx.saved_tensors
         dparts, ddt = grads[:-1], grads[-1]
         d_z, split = ctx.d_z, ctx.xbc_split
         d_xbc = sum(split)
@@ -58,9 +60,8 @@ class _SplitConv1dFn(torch.autograd.Function):
                 g = g.contiguous()
             pieces.append(g)
         need_dinit = initial_states is not None and ctx.needs_input_grad[4]
-        dweight, dbias, dinit = _bwd_split(zxbcdt[..., d_z:d_z + d_xbc], weight, bias, seq_idx,
-                                           initial_states, pieces, need_dinit, ctx.silu,
-                                           dzx[..., d_z:d_z + d_xbc])
+        dweight, dbias, dinit = _bwd_split(xbc, weight, bias, seq_idx, initial_states, pieces,
+                                           need_dinit, ctx.silu, dzx[..., d_z:d_z + d_xbc])
         return (dzx, dweight, dbias if bias is not None else None, None,
                 dinit if need_dinit else None, None, None, None)
 

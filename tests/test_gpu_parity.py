@@ -194,7 +194,8 @@ def test_generic_width(cc, W, dt):
 
 @pytest.mark.parametrize("W", [4, 12])
 def test_generic_width_seq(cc, W):
-    check_vs_oracle(cc, 2, 140, 40, W, torch.bfloat16, has_bias=True, silu=True, has_init=True,
+    # D = 36: rows of 72 bytes keep these on the generic kernels (no aligned copy helps).
+    check_vs_oracle(cc, 2, 140, 36, W, torch.bfloat16, has_bias=True, silu=True, has_init=True,
                     has_seq=True, ret_final=False, dfinal=False, need_dinit=True, seed=3 + W,
                     x_layout="row_pad1")
 
