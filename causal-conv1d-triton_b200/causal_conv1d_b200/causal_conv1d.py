@@ -311,7 +311,7 @@ def causal_conv1d_fn(
         assert return_final_states, "final_states_out requires return_final_states=True"
     _check_inputs(x, weight, bias, seq_idx, initial_states)
 
-    x = _tma_layout(_channels_contiguous(x), weight.shape[1])
+    x = _channels_contiguous(x)
     weight = weight.contiguous()
     bias = bias.contiguous() if bias is not None else None
     seq_idx = seq_idx.to(torch.int32).contiguous() if seq_idx is not None else None
@@ -322,6 +322,9 @@ def causal_conv1d_fn(
         t is not None and t.requires_grad for t in (x, weight, bias, initial_states)
     )
     if needs_grad:
+        # The forward reads any layout; the backward's kernels need 16-byte aligned x, so a
+        # misaligned x is copied once here and the copy is what the backward keeps.
+        x = _tma_layout(x, weight.shape[1])
         result = _CausalConv1dFn.apply(
             x, weight, bias, seq_idx, initial_states, return_final_states, silu
         )

@@ -490,10 +490,15 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
 
   const int es = elem_size(x_dtype);
   const int wt = tma_width(W);
-  if (wt > 0 && tma_layout_ok(x, stride_x_batch, stride_x_time, B, D, es)) {
+  // The tile kernel runs with TMA loads when x's layout allows, else with plain loads (its output
+  // vector stores need rows of a multiple of 8 bytes); other shapes take the generic kernel.
+  const bool tma_ok = tma_layout_ok(x, stride_x_batch, stride_x_time, B, D, es);
+  if (wt > 0 && (tma_ok || (D * es) % 8 == 0)) {
     const KernelInfo k = fwd_tma_for(x_dtype, wt, seq_idx != nullptr, silu != 0);
     FwdParams p{};
-    if (encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, k.d_tile, k.t_tile + wt - 1)) {
+    p.plain = tma_ok ? 0 : 1;
+    if (p.plain || encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, k.d_tile,
+                             k.t_tile + wt - 1)) {
       int occ = 0;
       CC1D_TRY(occupancy(k, k.smem, dev, &occ));  // also raises the kernel's dynamic shared memory limit
       p.x = x, p.weight = weight, p.bias = bias, p.init = initial_states, p.seq = seq_idx;

@@ -82,6 +82,7 @@ struct alignas(64) FwdParams {
   int W;               // true width: the template width less any leading zero taps
   int n_tt, n_db;      // time tiles per row, channel blocks
   int w_dtype, b_dtype, init_dtype;
+  int plain;           // 1: fill the tile with plain loads (x's base or strides rule out TMA)
 };
 
 // Sequence id of row t of batch row `srow` with the reference's conventions (causal_conv1d.py:
@@ -233,7 +234,30 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   const int t0 = tt * C::T_TILE;
   const int rg = threadIdx.x / C::LANES_D, lane = threadIdx.x % C::LANES_D;
 
-  if (threadIdx.x == 0) {
+  if (p.plain) {
+    // Layouts a tensor map cannot describe (base or batch/time strides not 16-byte multiples): the
+    // threads fill the same tile with element loads, 8 rows in flight per thread, rows outside
+    // [0, T) and channels outside [0, D) as zeros, as the TMA unit would.
+    constexpr int ROWS_PER_PASS = C::CONSUMERS / DT > 0 ? C::CONSUMERS / DT : 1;
+    const int c = threadIdx.x % DT, r_first = threadIdx.x / DT;
+    const int dd = db * DT + c;
+    const T* xrow = static_cast<const T*>(p.x) + static_cast<int64_t>(b) * p.sxb + dd;
+    T* trow = reinterpret_cast<T*>(tile) + c;
+    const T zero = from_f<T>(0.0f);
+    for (int r0 = r_first; r0 < L::XROWS; r0 += 8 * ROWS_PER_PASS) {
+      T v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int r = r0 + u * ROWS_PER_PASS, t = t0 - PAD + r;
+        v[u] = (r < L::XROWS && t >= 0 && t < p.T && dd < p.D) ? xrow[static_cast<int64_t>(t) * p.sxt] : zero;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int r = r0 + u * ROWS_PER_PASS;
+        if (r < L::XROWS) trow[r * DT] = v[u];
+      }
+    }
+  } else if (threadIdx.x == 0) {
     mbar_init(full, 1);
     fence_mbar_init();
     mbar_expect_tx(full, L::XBYTES);
@@ -258,8 +282,8 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   }
   if constexpr (SILU && FAST) halve_taps<W, NP>(w, bv);  // z below is h = z / 2
   const int pw = p.W - 1, off = W - p.W;  // true state rows; leading zero taps
-  __syncthreads();  // barrier initialised, seq window written
-  if (!mbar_wait(full, 0, p.status)) return;
+  __syncthreads();  // barrier initialised (or tile filled), seq window written
+  if (!p.plain && !mbar_wait(full, 0, p.status)) return;
 
   const T* xt = reinterpret_cast<const T*>(tile) + lane * CPT;  // local row r <-> global row t0 - PAD + r
   const int rb = rg * R;  // local row of global row ts - PAD
@@ -323,7 +347,13 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
       const int src = p.T - pw + q;
       float2 v[NP];
       if (src >= 0) {
-        load_vec<T, CPT>(static_cast<const T*>(p.x) + b * p.sxb + src * p.sxt + d, v);
+        const T* xs = static_cast<const T*>(p.x) + b * p.sxb + src * p.sxt + d;
+        if (p.plain) {  // x may be only element-aligned here
+#pragma unroll
+          for (int i2 = 0; i2 < NP; ++i2) v[i2] = make_float2(to_f(xs[2 * i2]), to_f(xs[2 * i2 + 1]));
+        } else {
+          load_vec<T, CPT>(xs, v);
+        }
       } else if (p.init != nullptr) {
         load_state_row<NP>(p.init, p.init_dtype, static_cast<int64_t>(b) * pw + src + pw, p.D, d, v);
       } else {

@@ -321,3 +321,42 @@ def test_sharded_fn_single_rank_matches_api(cc):
         res.append([out, x.grad, w.grad, b.grad, i.grad])
     for a, c in zip(*res):
         assert torch.equal(a, c)
+
+
+@pytest.mark.parametrize("x_layout", ["offset1", "row_pad1", "batch_gap"])
+@pytest.mark.parametrize("dt,W", [(torch.bfloat16, 4), (torch.bfloat16, 8), (torch.float16, 12), (torch.float32, 4)])
+def test_plain_load_forward_equals_tma(cc, x_layout, dt, W):
+    """The forward on a layout a tensor map cannot describe (its tile filled with plain loads)
+    gives the same bits as on a contiguous copy (tile filled by TMA): with initial and final
+    states, and with seq_idx."""
+    g = torch.Generator().manual_seed(W)
+    B, T, D = 3, 200, 136
+    x = torch.randn(B, T, D, generator=g).to(dt).to(DEV)
+    w = (torch.randn(D, W, generator=g) / W**0.5).to(DEV)
+    b = (torch.randn(D, generator=g) * 0.3).to(DEV)
+    init = torch.randn(B, W - 1, D, generator=g).to(dt).to(DEV)
+    seq = torch.cat([torch.zeros(B, 70), torch.ones(B, 100), torch.full((B, 30), -1.0)], 1).to(torch.int32).to(DEV)
+    xv = layout(x, x_layout)
+    with torch.no_grad():
+        got = cc.causal_conv1d_fn(xv, w, b, initial_states=init, return_final_states=True, activation="silu")
+        want = cc.causal_conv1d_fn(x, w, b, initial_states=init, return_final_states=True, activation="silu")
+        assert torch.equal(got[0], want[0]) and torch.equal(got[1], want[1])
+        got = cc.causal_conv1d_fn(xv, w, b, seq_idx=seq, initial_states=init, activation="silu")
+        want = cc.causal_conv1d_fn(x, w, b, seq_idx=seq, initial_states=init, activation="silu")
+        assert torch.equal(got, want)
+
+
+def test_plain_load_forward_rows_of_8_bytes(cc):
+    """D = 36 bf16 (72-byte rows: no tensor map, plain-load tile) against the oracle."""
+    g = torch.Generator().manual_seed(36)
+    B, T, D, W = 2, 150, 36, 4
+    x = torch.randn(B, T, D, generator=g).to(torch.bfloat16)
+    w = torch.randn(D, W, generator=g) * 0.5
+    b = torch.randn(D, generator=g) * 0.3
+    init = torch.randn(B, W - 1, D, generator=g).to(torch.bfloat16)
+    with torch.no_grad():
+        out, fin = cc.causal_conv1d_fn(x.to(DEV), w.to(DEV), b.to(DEV), initial_states=init.to(DEV),
+                                       return_final_states=True, activation="silu")
+    ro, rf = oracle.fwd(x, w, b, init, None, silu=True, return_final_states=True)
+    assert_close(out.cpu(), torch.from_numpy(ro).to(torch.bfloat16).float(), torch.bfloat16, "out")
+    assert_bitexact(fin.cpu().float(), torch.from_numpy(rf).to(torch.bfloat16).float(), "final_states")
