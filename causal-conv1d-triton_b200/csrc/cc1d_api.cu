@@ -120,6 +120,14 @@ int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
 // Whether a (B, T, D) channels-last tensor at `ptr` with batch/time strides (in elements) can be
 // read by the TMA kernels: 16-byte aligned base and strides, and rows of out/dx (D elements)
 // that are whole 16-byte vectors.
+// The backward walk's plain mode copies 8-byte chunks: base, strides and rows 8-byte multiples.
+bool chunk_layout_ok(const void* ptr, int64_t sb, int64_t st, int64_t B, int64_t D, int es) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 8 != 0) return false;
+  if (st <= 0 || (st * es) % 8 != 0) return false;
+  if (B > 1 && (sb <= 0 || (sb * es) % 8 != 0)) return false;
+  return (D * es) % 8 == 0;
+}
+
 bool tma_layout_ok(const void* ptr, int64_t sb, int64_t st, int64_t B, int64_t D, int es) {
   if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0) return false;
   if (st <= 0 || (st * es) % 16 != 0) return false;
@@ -157,15 +165,15 @@ int tma_width(int64_t W) {
   return 0;
 }
 
-KernelInfo fwd_tma_for(int dtype, int W, bool seq, bool silu) {
-  if (dtype == kBF16) return fwd_tma_info<__nv_bfloat16>(W, seq, silu);
-  if (dtype == kF16) return fwd_tma_info<__half>(W, seq, silu);
-  return fwd_tma_info<float>(W, seq, silu);
+KernelInfo fwd_tma_for(int dtype, int W, bool seq, bool silu, bool plain) {
+  if (dtype == kBF16) return fwd_tma_info<__nv_bfloat16>(W, seq, silu, plain);
+  if (dtype == kF16) return fwd_tma_info<__half>(W, seq, silu, plain);
+  return fwd_tma_info<float>(W, seq, silu, plain);
 }
-KernelInfo bwd_tma_for(int dtype, int W, bool seq, bool silu) {
-  if (dtype == kBF16) return bwd_tma_info<__nv_bfloat16>(W, seq, silu);
-  if (dtype == kF16) return bwd_tma_info<__half>(W, seq, silu);
-  return bwd_tma_info<float>(W, seq, silu);
+KernelInfo bwd_tma_for(int dtype, int W, bool seq, bool silu, bool plain) {
+  if (dtype == kBF16) return bwd_tma_info<__nv_bfloat16>(W, seq, silu, plain);
+  if (dtype == kF16) return bwd_tma_info<__half>(W, seq, silu, plain);
+  return bwd_tma_info<float>(W, seq, silu, plain);
 }
 KernelInfo fwd_generic_for(int dtype, int W) {
   if (dtype == kBF16) return fwd_generic_info<__nv_bfloat16>(W);
@@ -197,6 +205,7 @@ int check_sizes(int64_t B, int64_t T, int64_t D, int64_t W) {
 // Launch plan of the backward: which kernel, how many CTAs, how many partial rows.
 struct BwdPlan {
   bool tma = false;
+  bool plain = false;  // TMA-path kernels with the stage copied by cp.async (see BwdWalkParams)
   int wt = 0;     // template width of the TMA kernels (0: generic path)
   KernelInfo k;
   int max_smem = 0;
@@ -213,16 +222,20 @@ int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t sy
   const int es = elem_size(x_dtype);
   pl->wt = tma_width(W);
   pl->tma = pl->wt > 0 && tma_layout_ok(x, sxb, sxt, B, D, es) && tma_layout_ok(dy, syb, syt, B, D, es);
+  if (!pl->tma && pl->wt > 0 && chunk_layout_ok(x, sxb, sxt, B, D, es) && chunk_layout_ok(dy, syb, syt, B, D, es)) {
+    pl->tma = true;
+    pl->plain = true;
+  }
   int occ = 0;
   if (pl->tma) {
-    pl->k = bwd_tma_for(x_dtype, pl->wt, seq, silu);
+    pl->k = bwd_tma_for(x_dtype, pl->wt, seq, silu, pl->plain);
     pl->max_smem = pl->k.smem;
     // The partial count must not depend on seq_idx or the activation (the workspace query sees
     // neither): size the grid by the lowest occupancy of the four variants, all of which cover the
     // same channels per CTA.
     occ = 1 << 30;
     for (int v = 0; v < 4; ++v) {
-      const KernelInfo kv = bwd_tma_for(x_dtype, pl->wt, (v & 1) != 0, (v & 2) != 0);
+      const KernelInfo kv = bwd_tma_for(x_dtype, pl->wt, (v & 1) != 0, (v & 2) != 0, pl->plain);
       if (kv.d_tile != pl->k.d_tile) return CC1D_ERR_INVALID;
       int o = 0;
       CC1D_TRY(occupancy(kv, kv.smem, dev, &o));
@@ -323,7 +336,7 @@ int bwd_impl(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
     // Every piece and dx must suit the TMA walk: piece boundaries on channel blocks, 16-byte
     // aligned bases and strides (dx is written as 8-byte vectors at these strides).
     const int es = elem_size(x_dtype);
-    bool ok = pl.tma && reinterpret_cast<uintptr_t>(dx) % 16 == 0 && stride_dx_time >= D &&
+    bool ok = pl.tma && !pl.plain && reinterpret_cast<uintptr_t>(dx) % 16 == 0 && stride_dx_time >= D &&
               (stride_dx_time * es) % 16 == 0 && (B == 1 || (stride_dx_batch * es) % 16 == 0);
     int64_t c0 = 0;
     for (int i = 0; ok && i < n_pieces; ++i) {
@@ -341,11 +354,17 @@ int bwd_impl(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
     BwdWalkParams p{};
     const int PADi = pl.wt - 1;  // halo rows of the template width
     const int box_d = pl.k.box_d;  // one channel block per consumer warp
-    bool maps = encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, box_d, pl.k.t_tile + PADi);
+    // Plain mode (layout beyond a tensor map, see plan_bwd): no maps; the producer copies chunks.
+    bool maps = pl.plain ||
+                encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, box_d, pl.k.t_tile + PADi);
+    p.x = x, p.dy = pieces[0].ptr;
+    p.sxb = stride_x_batch, p.sxt = stride_x_time;
+    p.syb = pieces[0].stride_batch, p.syt = pieces[0].stride_time;
     int64_t c_end = 0;
     for (int i = 0; maps && i < n_pieces; ++i) {
-      maps = encode_3d(&p.tmap_dy[i], pieces[i].ptr, x_dtype, B, T, pieces[i].channels, pieces[i].stride_batch,
-                       pieces[i].stride_time, box_d, pl.k.t_tile);
+      if (!pl.plain)
+        maps = encode_3d(&p.tmap_dy[i], pieces[i].ptr, x_dtype, B, T, pieces[i].channels, pieces[i].stride_batch,
+                         pieces[i].stride_time, box_d, pl.k.t_tile);
       c_end += pieces[i].channels;
       p.dy_end[i] = static_cast<int>(c_end);
     }
@@ -494,10 +513,9 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
   // vector stores need rows of a multiple of 8 bytes); other shapes take the generic kernel.
   const bool tma_ok = tma_layout_ok(x, stride_x_batch, stride_x_time, B, D, es);
   if (wt > 0 && (tma_ok || (D * es) % 8 == 0)) {
-    const KernelInfo k = fwd_tma_for(x_dtype, wt, seq_idx != nullptr, silu != 0);
+    const KernelInfo k = fwd_tma_for(x_dtype, wt, seq_idx != nullptr, silu != 0, !tma_ok);
     FwdParams p{};
-    p.plain = tma_ok ? 0 : 1;
-    if (p.plain || encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, k.d_tile,
+    if (!tma_ok || encode_3d(&p.tmap_x, x, x_dtype, B, T, D, stride_x_batch, stride_x_time, k.d_tile,
                              k.t_tile + wt - 1)) {
       int occ = 0;
       CC1D_TRY(occupancy(k, k.smem, dev, &occ));  // also raises the kernel's dynamic shared memory limit

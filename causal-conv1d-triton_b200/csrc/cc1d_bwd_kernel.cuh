@@ -85,6 +85,11 @@ struct alignas(64) BwdWalkParams {
   void* dinit;          // (B, W-1, D) contiguous, dtype of init, or null
   float* partials;      // (P, W+1, D) fp32, P = gridDim.x / n_groups
   int64_t sdxb, sdxt;   // dx strides in elements (channel stride 1)
+  // PLAIN variant (x or dout not addressable by a tensor map, rows a multiple of 8 bytes): the
+  // producer copies the stage with 8-byte cp.async chunks from these, one dout piece only.
+  const void* x;
+  const void* dy;
+  int64_t sxb, sxt, syb, syt;
   int dy_end[kMaxDoutPieces];
   int n_dy;
   unsigned* status;
@@ -118,7 +123,7 @@ struct SegmentWalk {
   }
 };
 
-template <typename T, int W, bool SEQ, bool SILU>
+template <typename T, int W, bool SEQ, bool SILU, bool PLAIN>
 __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU>::MIN_CTAS)
     cc1d_bwd_walk_kernel(const __grid_constant__ BwdWalkParams p) {
   using C = BwdCfg<T, W, SILU>;
@@ -150,7 +155,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 32);
+      mbar_init(&full[s], PLAIN ? 64 : 32);  // producer lanes (+ their cp.async completions)
       mbar_init(&empty[s], C::WARPS);
     }
     fence_mbar_init();
@@ -160,7 +165,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == C::WARPS) {
     // ---------------- producer warp ----------------
-    if (lane == 0) {
+    if (lane == 0 && !PLAIN) {
       prefetch_tensormap(&p.tmap_x);
       for (int i = 0; i < p.n_dy; ++i) prefetch_tensormap(&p.tmap_dy[i]);
     }
@@ -175,7 +180,28 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
           break;
         }
         unsigned char* st = stage0 + s * C::STAGE_BYTES;
-        if (lane == 0) {
+        if constexpr (PLAIN) {
+          // The same stage layout from 8-byte chunks; chunks outside [0, T) or [0, D) are zeros.
+          constexpr int CPR = C::ROW_BYTES / 8, EPC = 8 / static_cast<int>(sizeof(T));
+          const unsigned char* xg = static_cast<const unsigned char*>(p.x);
+          const unsigned char* yg = static_cast<const unsigned char*>(p.dy);
+          for (int idx = lane; idx < nvb * C::XROWS * CPR; idx += 32) {
+            const int k = idx / (C::XROWS * CPR), rem = idx - k * (C::XROWS * CPR);
+            const int q = rem / CPR, jc = rem - q * CPR;
+            const int t = a_lo - PAD + q, c = (g * C::WARPS + k) * DT + jc * EPC;
+            const bool v = t >= 0 && t < T_ && c < p.D;
+            const int64_t off = v ? (b * p.sxb + t * p.sxt + c) * static_cast<int64_t>(sizeof(T)) : 0;
+            cp_async_8(st + (k * C::XROWS + q) * C::ROW_BYTES + jc * 8, xg + off, v ? 8 : 0);
+          }
+          for (int idx = lane; idx < nvb * RS * CPR; idx += 32) {
+            const int k = idx / (RS * CPR), rem = idx - k * (RS * CPR);
+            const int q = rem / CPR, jc = rem - q * CPR;
+            const int t = a_lo + q, c = (g * C::WARPS + k) * DT + jc * EPC;
+            const bool v = t < T_ && c < p.D;
+            const int64_t off = v ? (b * p.syb + t * p.syt + c) * static_cast<int64_t>(sizeof(T)) : 0;
+            cp_async_8(st + C::XBYTES + (k * RS + q) * C::ROW_BYTES + jc * 8, yg + off, v ? 8 : 0);
+          }
+        } else if (lane == 0) {
           mbar_expect_tx(&full[s], static_cast<uint32_t>(nvb) * (C::XROWS + RS) * C::ROW_BYTES);
           for (int k = 0; k < nvb; ++k) {
             const int c0 = (g * C::WARPS + k) * DT;
@@ -192,6 +218,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
           for (int r = lane; r < C::SROWS; r += 32) sq[r] = seq_at(srow, a_lo - PAD + r, T_, p.init != nullptr);
         }
         mbar_arrive(&full[s]);
+        if constexpr (PLAIN) cp_async_mbar_arrive_noinc(&full[s]);
       }
     });
     // Every copy this CTA issued must have landed before the CTA may exit.

@@ -180,6 +180,21 @@ __device__ __forceinline__ float2 dsilu2_of_half(float2 h, float2 dy) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// cp.async (8-byte chunks) with completion counted on an mbarrier
+// ---------------------------------------------------------------------------------------------
+// Copies 8 bytes global -> shared; src_bytes = 0 writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async_8(void* dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
+// One arrival on `bar` once every cp.async this thread issued before has completed (the arrival
+// counts toward the barrier's expected count).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
 // Conversions
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t u) {

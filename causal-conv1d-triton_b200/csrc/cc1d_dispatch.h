@@ -17,8 +17,9 @@ struct KernelInfo {
 };
 
 // TMA path, template widths 2..8, 12 and 16; fn is null for other widths.
-template <typename T> KernelInfo fwd_tma_info(int W, bool seq, bool silu);
-template <typename T> KernelInfo bwd_tma_info(int W, bool seq, bool silu);
+// `plain`: the variant that copies its tiles with plain loads / cp.async chunks instead of TMA.
+template <typename T> KernelInfo fwd_tma_info(int W, bool seq, bool silu, bool plain);
+template <typename T> KernelInfo bwd_tma_info(int W, bool seq, bool silu, bool plain);
 // Generic path, any width up to kGenericMaxWidth.
 template <typename T> KernelInfo fwd_generic_info(int W);
 template <typename T> KernelInfo bwd_generic_info(int W);

@@ -2,8 +2,8 @@
 #include "cc1d_inst_impl.cuh"
 
 namespace cc1d {
-template KernelInfo fwd_tma_info<__half>(int, bool, bool);
-template KernelInfo bwd_tma_info<__half>(int, bool, bool);
+template KernelInfo fwd_tma_info<__half>(int, bool, bool, bool);
+template KernelInfo bwd_tma_info<__half>(int, bool, bool, bool);
 template KernelInfo fwd_generic_info<__half>(int);
 template KernelInfo bwd_generic_info<__half>(int);
 }  // namespace cc1d

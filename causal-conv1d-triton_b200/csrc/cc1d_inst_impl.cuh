@@ -7,59 +7,67 @@
 namespace cc1d {
 namespace detail {
 
-template <typename T, int W, bool SEQ, bool SILU>
+template <typename T, int W, bool SEQ, bool SILU, bool PLAIN>
 KernelInfo fwd_tma_one() {
   using C = TileCfg<T, W>;
-  return {reinterpret_cast<const void*>(&cc1d_fwd_tma_kernel<T, W, SEQ, SILU>), FwdLayout<T, W, SEQ>::SMEM_BYTES,
+  return {reinterpret_cast<const void*>(&cc1d_fwd_tma_kernel<T, W, SEQ, SILU, PLAIN>), FwdLayout<T, W, SEQ>::SMEM_BYTES,
           C::CONSUMERS, C::D_TILE, C::T_TILE, C::D_TILE};
 }
-template <typename T, int W, bool SEQ, bool SILU>
+template <typename T, int W, bool SEQ, bool SILU, bool PLAIN>
 KernelInfo bwd_tma_one() {
   using C = BwdCfg<T, W, SILU>;
-  return {reinterpret_cast<const void*>(&cc1d_bwd_walk_kernel<T, W, SEQ, SILU>), C::SMEM_BYTES, C::THREADS, C::DG,
+  return {reinterpret_cast<const void*>(&cc1d_bwd_walk_kernel<T, W, SEQ, SILU, PLAIN>), C::SMEM_BYTES, C::THREADS, C::DG,
           C::RS, C::D_TILE};
 }
-template <typename T, int W>
-KernelInfo fwd_tma_w(bool seq, bool silu) {
-  if (seq) return silu ? fwd_tma_one<T, W, true, true>() : fwd_tma_one<T, W, true, false>();
-  return silu ? fwd_tma_one<T, W, false, true>() : fwd_tma_one<T, W, false, false>();
+template <typename T, int W, bool PLAIN>
+KernelInfo fwd_tma_p(bool seq, bool silu) {
+  if (seq) return silu ? fwd_tma_one<T, W, true, true, PLAIN>() : fwd_tma_one<T, W, true, false, PLAIN>();
+  return silu ? fwd_tma_one<T, W, false, true, PLAIN>() : fwd_tma_one<T, W, false, false, PLAIN>();
 }
 template <typename T, int W>
-KernelInfo bwd_tma_w(bool seq, bool silu) {
-  if (seq) return silu ? bwd_tma_one<T, W, true, true>() : bwd_tma_one<T, W, true, false>();
-  return silu ? bwd_tma_one<T, W, false, true>() : bwd_tma_one<T, W, false, false>();
+KernelInfo fwd_tma_w(bool seq, bool silu, bool plain) {
+  return plain ? fwd_tma_p<T, W, true>(seq, silu) : fwd_tma_p<T, W, false>(seq, silu);
+}
+template <typename T, int W, bool PLAIN>
+KernelInfo bwd_tma_p(bool seq, bool silu) {
+  if (seq) return silu ? bwd_tma_one<T, W, true, true, PLAIN>() : bwd_tma_one<T, W, true, false, PLAIN>();
+  return silu ? bwd_tma_one<T, W, false, true, PLAIN>() : bwd_tma_one<T, W, false, false, PLAIN>();
+}
+template <typename T, int W>
+KernelInfo bwd_tma_w(bool seq, bool silu, bool plain) {
+  return plain ? bwd_tma_p<T, W, true>(seq, silu) : bwd_tma_p<T, W, false>(seq, silu);
 }
 
 }  // namespace detail
 
 template <typename T>
-KernelInfo fwd_tma_info(int W, bool seq, bool silu) {
+KernelInfo fwd_tma_info(int W, bool seq, bool silu, bool plain) {
   switch (W) {
-    case 2: return detail::fwd_tma_w<T, 2>(seq, silu);
-    case 3: return detail::fwd_tma_w<T, 3>(seq, silu);
-    case 4: return detail::fwd_tma_w<T, 4>(seq, silu);
-    case 5: return detail::fwd_tma_w<T, 5>(seq, silu);
-    case 6: return detail::fwd_tma_w<T, 6>(seq, silu);
-    case 7: return detail::fwd_tma_w<T, 7>(seq, silu);
-    case 8: return detail::fwd_tma_w<T, 8>(seq, silu);
-    case 12: return detail::fwd_tma_w<T, 12>(seq, silu);
-    case 16: return detail::fwd_tma_w<T, 16>(seq, silu);
+    case 2: return detail::fwd_tma_w<T, 2>(seq, silu, plain);
+    case 3: return detail::fwd_tma_w<T, 3>(seq, silu, plain);
+    case 4: return detail::fwd_tma_w<T, 4>(seq, silu, plain);
+    case 5: return detail::fwd_tma_w<T, 5>(seq, silu, plain);
+    case 6: return detail::fwd_tma_w<T, 6>(seq, silu, plain);
+    case 7: return detail::fwd_tma_w<T, 7>(seq, silu, plain);
+    case 8: return detail::fwd_tma_w<T, 8>(seq, silu, plain);
+    case 12: return detail::fwd_tma_w<T, 12>(seq, silu, plain);
+    case 16: return detail::fwd_tma_w<T, 16>(seq, silu, plain);
     default: return {};
   }
 }
 
 template <typename T>
-KernelInfo bwd_tma_info(int W, bool seq, bool silu) {
+KernelInfo bwd_tma_info(int W, bool seq, bool silu, bool plain) {
   switch (W) {
-    case 2: return detail::bwd_tma_w<T, 2>(seq, silu);
-    case 3: return detail::bwd_tma_w<T, 3>(seq, silu);
-    case 4: return detail::bwd_tma_w<T, 4>(seq, silu);
-    case 5: return detail::bwd_tma_w<T, 5>(seq, silu);
-    case 6: return detail::bwd_tma_w<T, 6>(seq, silu);
-    case 7: return detail::bwd_tma_w<T, 7>(seq, silu);
-    case 8: return detail::bwd_tma_w<T, 8>(seq, silu);
-    case 12: return detail::bwd_tma_w<T, 12>(seq, silu);
-    case 16: return detail::bwd_tma_w<T, 16>(seq, silu);
+    case 2: return detail::bwd_tma_w<T, 2>(seq, silu, plain);
+    case 3: return detail::bwd_tma_w<T, 3>(seq, silu, plain);
+    case 4: return detail::bwd_tma_w<T, 4>(seq, silu, plain);
+    case 5: return detail::bwd_tma_w<T, 5>(seq, silu, plain);
+    case 6: return detail::bwd_tma_w<T, 6>(seq, silu, plain);
+    case 7: return detail::bwd_tma_w<T, 7>(seq, silu, plain);
+    case 8: return detail::bwd_tma_w<T, 8>(seq, silu, plain);
+    case 12: return detail::bwd_tma_w<T, 12>(seq, silu, plain);
+    case 16: return detail::bwd_tma_w<T, 16>(seq, silu, plain);
     default: return {};
   }
 }

@@ -82,7 +82,6 @@ struct alignas(64) FwdParams {
   int W;               // true width: the template width less any leading zero taps
   int n_tt, n_db;      // time tiles per row, channel blocks
   int w_dtype, b_dtype, init_dtype;
-  int plain;           // 1: fill the tile with plain loads (x's base or strides rule out TMA)
 };
 
 // Sequence id of row t of batch row `srow` with the reference's conventions (causal_conv1d.py:
@@ -211,7 +210,9 @@ __device__ __forceinline__ void load_state_row(const void* base, int dtype, int6
 // computes its 16 rows from shared memory and stores them. The grid holds every tile of the
 // tensor: on B200 a streaming copy through one TMA box per CTA over such a grid reaches ~6.7 TB/s,
 // while persistent CTAs looping over a multi-stage ring of the same boxes stay near 5.9 TB/s.
-template <typename T, int W, bool SEQ, bool SILU>
+// PLAIN: x's base or strides rule out a tensor map; the threads fill the same tile with plain loads
+// (separate instantiations, so the TMA variants keep their registers).
+template <typename T, int W, bool SEQ, bool SILU, bool PLAIN>
 __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>::MIN_CTAS)
     cc1d_fwd_tma_kernel(const __grid_constant__ FwdParams p) {
   using C = TileCfg<T, W>;
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   const int t0 = tt * C::T_TILE;
   const int rg = threadIdx.x / C::LANES_D, lane = threadIdx.x % C::LANES_D;
 
-  if (p.plain) {
+  if constexpr (PLAIN) {
     // Layouts a tensor map cannot describe (base or batch/time strides not 16-byte multiples): the
     // threads fill the same tile with element loads, 8 rows in flight per thread, rows outside
     // [0, T) and channels outside [0, D) as zeros, as the TMA unit would.
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   if constexpr (SILU && FAST) halve_taps<W, NP>(w, bv);  // z below is h = z / 2
   const int pw = p.W - 1, off = W - p.W;  // true state rows; leading zero taps
   __syncthreads();  // barrier initialised (or tile filled), seq window written
-  if (!p.plain && !mbar_wait(full, 0, p.status)) return;
+  if (!PLAIN && !mbar_wait(full, 0, p.status)) return;
 
   const T* xt = reinterpret_cast<const T*>(tile) + lane * CPT;  // local row r <-> global row t0 - PAD + r
   const int rb = rg * R;  // local row of global row ts - PAD
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
       float2 v[NP];
       if (src >= 0) {
         const T* xs = static_cast<const T*>(p.x) + b * p.sxb + src * p.sxt + d;
-        if (p.plain) {  // x may be only element-aligned here
+        if constexpr (PLAIN) {  // x may be only element-aligned here
 #pragma unroll
           for (int i2 = 0; i2 < NP; ++i2) v[i2] = make_float2(to_f(xs[2 * i2]), to_f(xs[2 * i2 + 1]));
         } else {

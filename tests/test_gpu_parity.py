@@ -360,3 +360,23 @@ def test_plain_load_forward_rows_of_8_bytes(cc):
     ro, rf = oracle.fwd(x, w, b, init, None, silu=True, return_final_states=True)
     assert_close(out.cpu(), torch.from_numpy(ro).to(torch.bfloat16).float(), torch.bfloat16, "out")
     assert_bitexact(fin.cpu().float(), torch.from_numpy(rf).to(torch.bfloat16).float(), "final_states")
+
+
+CHUNK = [(torch.bfloat16, 36, 4), (torch.bfloat16, 100, 2), (torch.bfloat16, 100, 8), (torch.float16, 36, 12),
+         (torch.float32, 34, 4)]
+
+
+@pytest.mark.parametrize("dt,D,W", CHUNK, ids=[f"{str(d)[6:]}-D{D}-W{W}" for d, D, W in CHUNK])
+@pytest.mark.parametrize("flags", ["bias_silu", "state_chain", "seq_init", "plain"])
+def test_backward_8_byte_rows(cc, dt, D, W, flags):
+    """Rows of 8-byte but not 16-byte multiples: no tensor map, the backward walk copies its stages
+    in 8-byte cp.async chunks (and the forward fills its tile with plain loads)."""
+    f = dict(has_bias=False, silu=False, has_init=False, has_seq=False, ret_final=False, dfinal=False,
+             need_dinit=False)
+    if flags == "bias_silu":
+        f.update(has_bias=True, silu=True)
+    elif flags == "state_chain":
+        f.update(has_bias=True, silu=True, has_init=True, ret_final=True, dfinal=True, need_dinit=True)
+    elif flags == "seq_init":
+        f.update(has_bias=True, silu=True, has_init=True, has_seq=True, need_dinit=True)
+    check_vs_oracle(cc, 3, 150, D, W, dt, seed=D + W + len(flags), **f)
