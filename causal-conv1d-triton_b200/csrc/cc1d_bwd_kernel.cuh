@@ -182,24 +182,31 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
         unsigned char* st = stage0 + s * C::STAGE_BYTES;
         if constexpr (PLAIN) {
           // The same stage layout from 8-byte chunks; chunks outside [0, T) or [0, D) are zeros.
-          constexpr int CPR = C::ROW_BYTES / 8, EPC = 8 / static_cast<int>(sizeof(T));
+          // Lane = chunk column (RPI rows per pass when a row segment has fewer chunks than lanes).
+          constexpr int CPR = C::ROW_BYTES / 8, EPC = 8 / static_cast<int>(sizeof(T)), RPI = 32 / CPR;
+          constexpr int64_t ES = sizeof(T);
+          const int jc = lane % CPR, qo = lane / CPR;
           const unsigned char* xg = static_cast<const unsigned char*>(p.x);
           const unsigned char* yg = static_cast<const unsigned char*>(p.dy);
-          for (int idx = lane; idx < nvb * C::XROWS * CPR; idx += 32) {
-            const int k = idx / (C::XROWS * CPR), rem = idx - k * (C::XROWS * CPR);
-            const int q = rem / CPR, jc = rem - q * CPR;
-            const int t = a_lo - PAD + q, c = (g * C::WARPS + k) * DT + jc * EPC;
-            const bool v = t >= 0 && t < T_ && c < p.D;
-            const int64_t off = v ? (b * p.sxb + t * p.sxt + c) * static_cast<int64_t>(sizeof(T)) : 0;
-            cp_async_8(st + (k * C::XROWS + q) * C::ROW_BYTES + jc * 8, xg + off, v ? 8 : 0);
-          }
-          for (int idx = lane; idx < nvb * RS * CPR; idx += 32) {
-            const int k = idx / (RS * CPR), rem = idx - k * (RS * CPR);
-            const int q = rem / CPR, jc = rem - q * CPR;
-            const int t = a_lo + q, c = (g * C::WARPS + k) * DT + jc * EPC;
-            const bool v = t < T_ && c < p.D;
-            const int64_t off = v ? (b * p.syb + t * p.syt + c) * static_cast<int64_t>(sizeof(T)) : 0;
-            cp_async_8(st + C::XBYTES + (k * RS + q) * C::ROW_BYTES + jc * 8, yg + off, v ? 8 : 0);
+          for (int k = 0; k < nvb; ++k) {
+            const int c = (g * C::WARPS + k) * DT + jc * EPC;
+            const bool cv = c < p.D;
+            const unsigned char* xcol = xg + (b * p.sxb + c) * ES;
+            const unsigned char* ycol = yg + (b * p.syb + c) * ES;
+            unsigned char* xdst = st + k * C::XROWS * C::ROW_BYTES + jc * 8;
+            unsigned char* ydst = st + C::XBYTES + k * RS * C::ROW_BYTES + jc * 8;
+#pragma unroll 4
+            for (int q = qo; q < C::XROWS; q += RPI) {
+              const int t = a_lo - PAD + q;
+              const bool v = cv && t >= 0 && t < T_;
+              cp_async_8(xdst + q * C::ROW_BYTES, v ? xcol + t * p.sxt * ES : xg, v ? 8 : 0);
+            }
+#pragma unroll 4
+            for (int q = qo; q < RS; q += RPI) {
+              const int t = a_lo + q;
+              const bool v = cv && t < T_;
+              cp_async_8(ydst + q * C::ROW_BYTES, v ? ycol + t * p.syt * ES : yg, v ? 8 : 0);
+            }
           }
         } else if (lane == 0) {
           mbar_expect_tx(&full[s], static_cast<uint32_t>(nvb) * (C::XROWS + RS) * C::ROW_BYTES);
