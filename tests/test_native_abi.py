@@ -134,3 +134,25 @@ def test_copy_channels_rejects_bad_arguments():
     assert lib.cc1d_copy_channels(None, 0, 0, None, 0, 0, 1, 1, 1, 3, None) == _native.CC1D_ERR_INVALID
     assert lib.cc1d_copy_channels(None, 0, 0, None, 0, 0, -1, 1, 1, 2, None) == _native.CC1D_ERR_INVALID
     assert lib.cc1d_copy_channels(None, 0, 0, None, 0, 0, 0, 8, 8, 2, None) == _native.CC1D_OK  # empty
+
+
+def test_tma_layout_routing():
+    """Host logic: a misaligned x whose rows are 16-byte multiples is copied once (contiguous,
+    16-byte aligned) for the TMA kernels; aligned tensors, rows of other sizes and widths above 16
+    are passed through unchanged."""
+    from causal_conv1d_b200.causal_conv1d import _tma_layout
+
+    x = torch.randn(2, 8, 16).to(torch.bfloat16)
+    assert _tma_layout(x, 4) is x
+    wide = torch.zeros(2, 8, 17, dtype=torch.bfloat16)
+    sl = wide[..., 1:]  # odd channel offset: base 2 bytes past alignment
+    y = _tma_layout(sl, 4)
+    assert y is not sl and y.is_contiguous() and y.data_ptr() % 16 == 0 and torch.equal(y, sl)
+    assert _tma_layout(sl, 17) is sl  # width beyond the TMA kernels
+    odd = torch.zeros(2, 8, 13, dtype=torch.bfloat16)[..., 1:]  # 12 channels: 24-byte rows
+    assert _tma_layout(odd, 4) is odd
+    leaf = torch.zeros(2, 8, 17, dtype=torch.bfloat16, requires_grad=True)
+    copied = _tma_layout(leaf[..., 1:], 4)  # misaligned view of a leaf: copied
+    assert copied.data_ptr() != leaf.data_ptr()
+    copied.float().sum().backward()  # the copy is differentiable
+    assert (leaf.grad[..., 1:] == 1).all() and (leaf.grad[..., 0] == 0).all()
