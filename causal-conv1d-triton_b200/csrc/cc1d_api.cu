@@ -1,5 +1,6 @@
 // C ABI of the causal depthwise conv1d library: argument checks, path selection (TMA kernels for
-// widths 2..16 on 16-byte-aligned layouts, generic kernels otherwise), tensor-map encoding, grid
+// widths 2..16 on 16-byte-aligned layouts, their plain-load / cp.async variants on layouts with
+// 8-byte rows, generic kernels otherwise), tensor-map encoding, grid
 // sizing from the measured occupancy and SM count, and the T == 0 cases. Declared in
 // include/causal_conv1d_b200.h, where each entry point names the reference launch it replaces.
 #include <cudaTypedefs.h>
