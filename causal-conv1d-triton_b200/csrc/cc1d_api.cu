@@ -268,6 +268,24 @@ int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t sy
   return CC1D_OK;
 }
 
+// Workspace bytes the backward of this problem needs (0 for an empty one), or the error code
+// cc1d_bwd would return for the same sizes, dtype and device. The plan does not depend on
+// seq_idx or the activation.
+int workspace_need(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t syb, int64_t syt, int64_t B,
+                   int64_t T, int64_t D, int64_t W, int x_dtype, int64_t* bytes) {
+  *bytes = 0;
+  if (!valid_dtype(x_dtype)) return CC1D_ERR_INVALID;
+  CC1D_TRY(check_sizes(B, T, D, W));
+  if (B == 0 || D == 0 || T == 0) return CC1D_OK;
+  DeviceInfo di;
+  int dev = 0;
+  CC1D_TRY(device_info(&di, &dev));
+  BwdPlan pl;
+  CC1D_TRY(plan_bwd(x, sxb, sxt, dy, syb, syt, B, T, D, W, x_dtype, false, false, di, dev, &pl));
+  *bytes = pl.ws_bytes;
+  return CC1D_OK;
+}
+
 template <typename T>
 const void* update_vec_for_width(int W) {
   switch (W) {
@@ -643,16 +661,11 @@ int cc1d_copy_channels(void* dst, int64_t dst_stride_batch, int64_t dst_stride_t
 int64_t cc1d_bwd_workspace_bytes(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* dout,
                                  int64_t stride_dout_batch, int64_t stride_dout_time, int64_t batch, int64_t seqlen,
                                  int64_t dim, int64_t width, int x_dtype) {
-  if (!valid_dtype(x_dtype) || check_sizes(batch, seqlen, dim, width) != CC1D_OK) return -1;
-  if (batch == 0 || dim == 0 || seqlen == 0) return 0;
-  DeviceInfo di;
-  int dev = 0;
-  if (device_info(&di, &dev) != CC1D_OK) return -1;
-  BwdPlan pl;
-  if (plan_bwd(x, stride_x_batch, stride_x_time, dout, stride_dout_batch, stride_dout_time, batch, seqlen, dim, width,
-               x_dtype, false, false, di, dev, &pl) != CC1D_OK)
+  int64_t bytes = 0;
+  if (workspace_need(x, stride_x_batch, stride_x_time, dout, stride_dout_batch, stride_dout_time, batch, seqlen, dim,
+                     width, x_dtype, &bytes) != CC1D_OK)
     return -1;
-  return pl.ws_bytes;
+  return bytes;
 }
 
 int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const void* weight, const void* bias,
@@ -713,7 +726,9 @@ int cc1d_bwd_split(const void* x, int64_t stride_x_batch, int64_t stride_x_time,
 //    stream, or events).
 //  - The first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress, with that device current; make that first call before any stream
-//    capture begins.
+//    capture begins. The address is kept for the life of the process, so cudaDeviceReset on a
+//    device after its first call is not supported (the module reloads and the array may move).
+//  - Errors are cc1d_bwd's: the same sizes, dtypes and device give the same code.
 // ---------------------------------------------------------------------------------------------
 namespace cc1d {
 namespace {
@@ -746,9 +761,10 @@ extern "C" int cc1d_bwd_noalloc(const void* x, int64_t stride_x_batch, int64_t s
                                 void* dx, void* dweight, void* dbias, void* dinit, float* grad_f32, int64_t batch,
                                 int64_t seqlen, int64_t dim, int64_t width, int x_dtype, int weight_dtype,
                                 int bias_dtype, int init_dtype, int silu, void* stream) {
-  const int64_t need = cc1d_bwd_workspace_bytes(x, stride_x_batch, stride_x_time, dout, stride_dout_batch,
-                                                stride_dout_time, batch, seqlen, dim, width, x_dtype);
-  if (need < 0) return CC1D_ERR_INVALID;
+  int64_t need = 0;
+  const int prc = cc1d::workspace_need(x, stride_x_batch, stride_x_time, dout, stride_dout_batch, stride_dout_time,
+                                       batch, seqlen, dim, width, x_dtype, &need);
+  if (prc != CC1D_OK) return prc;
   if (static_cast<uint64_t>(need) > cc1d::kNoAllocScratchBytes) return CC1D_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
   const int rc = cc1d::noalloc_scratch(&scratch);

@@ -284,7 +284,12 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   if constexpr (SILU && FAST) halve_taps<W, NP>(w, bv);  // z below is h = z / 2
   const int pw = p.W - 1, off = W - p.W;  // true state rows; leading zero taps
   __syncthreads();  // barrier initialised (or tile filled), seq window written
-  if (!PLAIN && !mbar_wait(full, 0, p.status)) return;
+  if (!PLAIN && !mbar_wait(full, 0, p.status)) {
+    // Gave up (status recorded). The tile copy may still be landing in this CTA's shared memory:
+    // wait for it once more, again bounded, before the CTA exits.
+    mbar_wait(full, 0, p.status);
+    return;
+  }
 
   const T* xt = reinterpret_cast<const T*>(tile) + lane * CPT;  // local row r <-> global row t0 - PAD + r
   const int rb = rg * R;  // local row of global row ts - PAD

@@ -138,7 +138,9 @@ int cc1d_bwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
  * CC1D_ERR_SCRATCH_LIMIT before any device work. All calls on a device share the array, so calls
  * that overlap on the GPU race; order them on one stream. Nothing in the array must start at zero.
  * The first call on each device looks up the array's address (cudaGetSymbolAddress) with that
- * device current; make it before any stream capture.
+ * device current; make it before any stream capture. The address is kept until the process exits,
+ * so cudaDeviceReset of a device after its first call is not supported. Error codes are those
+ * cc1d_bwd returns for the same arguments, plus CC1D_ERR_SCRATCH_LIMIT.
  */
 int cc1d_bwd_noalloc(const void* x, int64_t stride_x_batch, int64_t stride_x_time,
                      const void* weight, const void* bias, const void* initial_states,
@@ -198,7 +200,9 @@ int cc1d_copy_channels(void* dst, int64_t dst_stride_batch, int64_t dst_stride_t
 /*
  * Reads the device status word of the current device after synchronising it, and clears it when
  * `clear` is non-zero. Bit 0 set: a kernel gave up waiting on one of its pipeline barriers
- * (bounded at one second) and returned early, so its outputs are incomplete.
+ * (bounded at one second) and returned early, so its outputs are incomplete. The word's device
+ * address is looked up once per device and kept, so cudaDeviceReset after the library's first
+ * call on a device is not supported.
  */
 int cc1d_status(uint32_t* status, int clear);
 

@@ -5,19 +5,18 @@ cudaMalloc after start-up, a path where cudaMalloc/cudaFree could synchronise th
 code that reaches the library only through its C ABI with no device allocator) cannot hand
 cc1d_bwd a workspace. cc1d_bwd_noalloc keeps the partial sums in a fixed 8 MiB array inside the
 library instead. This test calls it through the C ABI and checks it against cc1d_bwd (given a
-workspace) on the same inputs, twice in a row, since every call reuses the same array; and checks
-that a problem too large for the array is refused before any device work.
+workspace) on the same inputs, twice in a row, since every call reuses the same array. Both run
+the same kernels with the same partial count and a fixed-order reduction, so the results must be
+identical bit for bit. It also checks that the device's free memory does not change across a
+call, that a problem too large for the array is refused before any device work, and that other
+errors come back with cc1d_bwd's own codes.
 
 The file name makes pytest collect it last, so a failure here comes after every other test ran.
 It passes on its own in a fresh process as well as after the other tests.
 """
 
-import ctypes
-
 import pytest
 import torch
-
-from _tol import assert_close, assert_close_sum
 
 pytestmark = pytest.mark.gpu
 
@@ -69,15 +68,16 @@ def test_noalloc_matches_workspace_backward_twice():
         assert rc == 0, lib.cc1d_error_string(rc)
 
         got = _outputs(x, w, b, init)
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
         rc = lib.cc1d_bwd_noalloc(*args_in, *[_p(t) for t in got], None,
                                   B, T, D, W, BF16, F32, F32, BF16, 1, stream)
         assert rc == 0, lib.cc1d_error_string(rc)
         torch.cuda.synchronize()
+        assert torch.cuda.mem_get_info()[0] == free_before, "the call changed the device's free memory"
 
-        assert_close(got[0], ref[0], "bf16", "dx")
-        assert_close_sum(got[1], ref[1], "bf16", "dweight")
-        assert_close_sum(got[2], ref[2], "bf16", "dbias")
-        assert_close(got[3], ref[3], "bf16", "dinit")
+        for name, a, e in zip(("dx", "dweight", "dbias", "dinit"), got, ref):
+            assert torch.equal(a, e), f"{name}: cc1d_bwd_noalloc differs from cc1d_bwd"
 
 
 def test_noalloc_rejects_problems_above_its_scratch():
@@ -100,3 +100,27 @@ def test_noalloc_rejects_problems_above_its_scratch():
                               torch.cuda.current_stream().cuda_stream)
     assert rc == _native.CC1D_ERR_SCRATCH_LIMIT
     assert b"8 MiB" in lib.cc1d_error_string(rc)
+
+
+def test_noalloc_returns_cc1d_bwd_error_codes():
+    from causal_conv1d_b200 import _native
+
+    lib = _native.lib
+    B, T, D = 1, 16, 64
+    x = torch.zeros(B, T, D, device=DEV, dtype=torch.bfloat16)
+    dy = torch.zeros_like(x)
+    dx = torch.empty_like(x)
+    stream = torch.cuda.current_stream().cuda_stream
+    for W, want in ((257, _native.CC1D_ERR_UNSUPPORTED), (1, _native.CC1D_ERR_INVALID)):
+        w = torch.zeros(D, max(W, 1), device=DEV)
+        dw = torch.empty_like(w)
+        rc = lib.cc1d_bwd_noalloc(x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), None, None,
+                                  None, dy.data_ptr(), dy.stride(0), dy.stride(1), None,
+                                  dx.data_ptr(), dw.data_ptr(), None, None, None, B, T, D, W,
+                                  BF16, F32, F32, F32, 0, stream)
+        ws = torch.empty(1024, device=DEV)
+        rc_ws = lib.cc1d_bwd(x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), None, None,
+                             None, dy.data_ptr(), dy.stride(0), dy.stride(1), None, dx.data_ptr(),
+                             dw.data_ptr(), None, None, None, ws.data_ptr(), 4096, B, T, D, W,
+                             BF16, F32, F32, F32, 0, stream)
+        assert rc == want == rc_ws, (W, rc, rc_ws)
