@@ -22,8 +22,14 @@ Algorithmic bytes per call (bf16 x/out/dout/dx = 2 B, fp32 weight/bias):
 
 --impl reference times the reference algorithm on the host CPU: the oracle (oracle/, a C
 restatement of the reference's per-element algorithm; the reference itself is Python/Triton and has
-no CPU implementation), with all host threads, on a bounded sample of the workload per step.
---impl triton times the reference's own Triton kernels (baseline/_ref) on the same B200.
+no CPU implementation), with all host threads; each step is one whole batch row (T x D) forward +
+backward, the same sample the `cpu_baseline` leg of the default arm times.
+--impl triton times the reference's own Triton kernels (baseline/_ref) on the same B200; at N=1 the
+default arm runs it in a subprocess on the same workload and embeds it as `triton_reference`.
+
+At every N the default arm also runs BASELINE config 5 strong-scaled (`cfg5_sharded`: B=64 T=8192
+D=8192 W=8 bias+SiLU split over the N ranks, NCCL all-reduce of dweight||dbias included) and checks
+the sharded weight/bias gradient against the single-GPU full-batch gradient computed on rank 0.
 """
 
 from __future__ import annotations
@@ -49,8 +55,9 @@ NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the backward kernel at
-# this workload (B=8, T=32768, D=1024, W=4, bias+SiLU), from the ncu launch list in
-# profiles/bwd_walk_kernel_cfg2.md; it scales with the B*T rows processed.
+# this workload (B=8, T=32768, D=1024, W=4, bias+SiLU), read from an ncu launch list of this
+# command on a B200; it scales with the B*T rows processed. Re-captured after each change of the
+# backward kernel.
 BWD_DRAM_BYTES_PER_LAUNCH = 1089.6e6 + 509.0e6
 BWD_DRAM_ROWS = 8 * 32768
 
@@ -68,6 +75,10 @@ def parse():
     ap.add_argument("--no-bias-silu", action="store_true", help="the no-bias/no-activation mode")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget")
+    ap.add_argument("--cfg5-steps", type=int, default=10,
+                    help="timed steps of the strong-scaled config-5 sub-record (0 skips it)")
+    ap.add_argument("--no-triton-arm", action="store_true",
+                    help="skip the embedded reference-Triton run at N=1")
     ap.add_argument("--sweep", action="store_true",
                     help="time every BASELINE config through both implementations' public APIs "
                          "(ours and the reference's Triton kernels) and print one JSON line each")
@@ -183,56 +194,99 @@ def same_size_copy_gbs(x, stream, reps=20):
     return 2 * x.numel() * x.element_size() * reps / (s.elapsed_time(e) * 1e-3) / 1e9
 
 
-def cpu_sample_gbs(w, b, x, dy, silu, seconds, nthreads=0, rows=None):
-    """Times the oracle (fwd + bwd) on batch row 0 (optionally its first `rows` time rows) until
-    `seconds` have passed; returns (GB/s of algorithmic bytes, sample description, reps)."""
-    from oracle import oracle
+class CpuSample:
+    """The CPU sample both CPU timings use: batch row 0 of the workload (all T rows, all D
+    channels), forward + backward through the oracle, fp32 copies prepared once."""
 
-    xs = x[:1] if rows is None else x[:1, :rows]
-    dys = dy[:1] if rows is None else dy[:1, :rows]
-    xs32, dys32 = xs.float().numpy(), dys.float().numpy()
-    _, T, D = xs.shape
-    W = w.shape[1]
-    fb, bb = algo_bytes(1, T, D, W)
+    def __init__(self, x, w, b, dy, silu, nthreads):
+        from oracle import oracle
+
+        self.oracle = oracle
+        self.xs, self.dys = x[:1].float().numpy(), dy[:1].float().numpy()
+        self.w, self.b, self.silu, self.nthreads = w, b, silu, nthreads
+        _, self.T, self.D = self.xs.shape
+        self.W = w.shape[1]
+        fb, bb = algo_bytes(1, self.T, self.D, self.W)
+        self.bytes = fb + bb
+        self.desc = f"batch row 0 (T={self.T}, D={self.D}, W={self.W}), fwd+bwd per rep"
+
+    def step(self):
+        o = self.oracle
+        o.fwd(self.xs, self.w, self.b, None, None, silu=self.silu, nthreads=self.nthreads)
+        o.bwd(self.xs, self.w, self.b, None, None, self.dys, None, False, silu=self.silu,
+              nthreads=self.nthreads)
+
+
+def cpu_sample_gbs(w, b, x, dy, silu, seconds, nthreads=0):
+    """Times the oracle (fwd + bwd) on the CPU sample until `seconds` have passed (after one
+    untimed rep); returns (GB/s of algorithmic bytes, sample description, reps)."""
+    cs = CpuSample(x, w, b, dy, silu, nthreads)
+    cs.step()
     reps, t0 = 0, time.perf_counter()
     while True:
-        oracle.fwd(xs32, w, b, None, None, silu=silu, nthreads=nthreads)
-        oracle.bwd(xs32, w, b, None, None, dys32, None, False, silu=silu, nthreads=nthreads)
+        cs.step()
         reps += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    return (fb + bb) * reps / el / 1e9, f"batch row 0, T={T}, D={D}: fwd+bwd x{reps} in {el:.1f} s", reps
+    return cs.bytes * reps / el / 1e9, f"{cs.desc}: x{reps} in {el:.1f} s", reps
+
+
+def torch_conv1d_cpu_gbs(w, b, x, dy, silu, seconds):
+    """The reference semantics as PyTorch F.conv1d(groups=D) with left padding on the host cores
+    (forward + autograd backward, bf16 as the workload), on batch row 0: the CPU baseline the
+    task names beside the port. Returns (GB/s of algorithmic bytes, threads, sample)."""
+    import torch.nn.functional as F
+
+    T, D = x.shape[1], x.shape[2]
+    W = w.shape[1]
+    xl = x[:1].clone().requires_grad_(True)
+    wl = w.to(torch.bfloat16).clone().requires_grad_(True)
+    bl = b.to(torch.bfloat16).clone().requires_grad_(True) if b is not None else None
+    dyl = dy[:1]
+
+    def step():
+        y = F.conv1d(F.pad(xl.transpose(1, 2), (W - 1, 0)), wl[:, None, :], bl, groups=D)
+        if silu:
+            y = F.silu(y)
+        y.transpose(1, 2).backward(dyl)
+        xl.grad = wl.grad = None
+        if bl is not None:
+            bl.grad = None
+
+    step()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    fb, bb = algo_bytes(1, T, D, W)
+    sample = (f"batch row 0 (T={T}, D={D}, W={W}), bf16 F.conv1d(F.pad(x.transpose(1, 2), (W-1, 0)), "
+              f"weight[:, None], bias, groups=D){' + SiLU' if silu else ''} + autograd backward: "
+              f"x{reps} in {el:.1f} s")
+    return (fb + bb) * reps / el / 1e9, torch.get_num_threads(), sample
 
 
 def run_reference_cpu(args):
-    """--impl reference: the reference algorithm on the host cores (the oracle port)."""
+    """--impl reference: the reference algorithm on the host cores (the oracle port), each step
+    the same CPU sample the default arm's cpu_baseline times (one whole batch row)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import oracle
-
     B, T, D, W = args.batch, args.seqlen, args.dim, args.width
     bias_silu = not args.no_bias_silu
     x, w, b, dy = make_inputs(B, T, D, W, bias_silu)
-    rows = min(T, 2048)  # bounded sample per step: batch row 0, first 2048 time rows
-    xs, dys = x[:1, :rows].float().numpy(), dy[:1, :rows].float().numpy()
-    fb, bb = algo_bytes(1, rows, D, W)
-
     threads = os.cpu_count()
-
-    def step():
-        oracle.fwd(xs, w, b, None, None, silu=bias_silu, nthreads=threads)
-        oracle.bwd(xs, w, b, None, None, dys, None, False, silu=bias_silu, nthreads=threads)
-
+    cs = CpuSample(x, w, b, dy, bias_silu, threads)
     for _ in range(args.warmup):
-        step()
+        cs.step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        cs.step()
     el = time.perf_counter() - t0
-    gbs = (fb + bb) * args.steps / el / 1e9
-    sample = f"per step: batch row 0, T[0:{rows}], D={D}, W={W}, fwd+bwd"
+    gbs = cs.bytes * args.steps / el / 1e9
     print(json.dumps({
         "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3, "higher_is_better": True,
@@ -240,7 +294,7 @@ def run_reference_cpu(args):
         "data": "synthetic, seed 0",
         "config": workload_config(args),
         "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": f"per step: {cs.desc}"},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -631,21 +685,38 @@ def main():
     else:
         from causal_conv1d_b200.causal_conv1d import _bwd, _fwd
 
-        grad_buf = torch.zeros(D * (W + 1), device=dev, dtype=torch.float32) if world > 1 else None
+        # Two fp32 dweight||dbias buffers: step i's all-reduce runs on NCCL's stream while step
+        # i+1's forward runs; step i+2's backward, which rewrites the buffer, waits for it first.
+        grad_buf = [torch.zeros(D * (W + 1), device=dev, dtype=torch.float32) for _ in range(2)] if world > 1 else None
+        pending = [None, None]
+        n_bwd = [0]
 
         def fwd():
             return _fwd(x, w, b, None, None, None, bias_silu)
 
         def bwd():
-            r = _bwd(x, w, b, None, None, dy, None, False, bias_silu, grad_f32=grad_buf)
-            if world > 1:
-                dist.all_reduce(grad_buf)
+            if world == 1:
+                return _bwd(x, w, b, None, None, dy, None, False, bias_silu)
+            k = n_bwd[0] % 2
+            n_bwd[0] += 1
+            if pending[k] is not None:
+                pending[k].wait()  # the compute stream waits for the all-reduce that last read buf k
+            r = _bwd(x, w, b, None, None, dy, None, False, bias_silu, grad_f32=grad_buf[k])
+            pending[k] = dist.all_reduce(grad_buf[k], async_op=True)
             return r
 
     stream = torch.cuda.current_stream(dev)
+    def join():
+        if args.impl != "triton" and world > 1:
+            for k in range(2):
+                if pending[k] is not None:
+                    pending[k].wait()
+                    pending[k] = None
+
     for _ in range(args.warmup):
         fwd()
         bwd()
+    join()
     torch.cuda.synchronize(dev)
 
     n_ev = args.steps
@@ -665,6 +736,7 @@ def main():
         ev[i][1].record(stream)
         bwd()
         ev[i][2].record(stream)
+    join()
     end.record(stream)
     torch.cuda.synchronize(dev)
     sampler.mark_end()
@@ -719,20 +791,195 @@ def main():
         "frac_of_copy_same_size": bwd_gbs / copy_gbs,
     }
 
+    if world > 1:
+        line["allreduce_us"] = allreduce_us(dist, grad_buf[0].clone(), stream)
+
     # End to end through the public API, host buffers in and out.
     line["e2e"] = e2e(args, dev, x_h, w_h, b_h, dy_h, bias_silu, world, dist)
 
+    if args.cfg5_steps > 0:
+        del x, dy
+        torch.cuda.empty_cache()
+        line["cfg5_sharded"] = cfg5_sharded(args, dev, world, rank, dist)
+
     if rank == 0:
-        if world == 1:  # the CPU baseline is measured at N = 1 only
+        if world == 1:  # the CPU baselines and the reference's Triton arm are measured at N = 1 only
             threads = os.cpu_count()
             gbs, sample, _ = cpu_sample_gbs(w_h, b_h, x_h, dy_h, bias_silu, args.cpu_seconds,
                                             nthreads=threads)
             line["cpu_baseline"] = {"value": gbs, "unit": "GB/s", "cores": threads,
                                     "kind": "port", "sample": sample}
+            tg, tthreads, tsample = torch_conv1d_cpu_gbs(w_h, b_h, x_h, dy_h, bias_silu,
+                                                         args.cpu_seconds / 2)
+            line["cpu_baseline_torch_conv1d"] = {"value": tg, "unit": "GB/s", "cores": os.cpu_count(),
+                                                 "threads": tthreads, "sample": tsample}
+            if not args.no_triton_arm:
+                line["triton_reference"] = triton_arm(args, line)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def allreduce_us(dist, buf, stream, reps=50):
+    """Device time of one blocking NCCL all-reduce (sum) of `buf` on its own, max over ranks."""
+    for _ in range(5):
+        dist.all_reduce(buf)
+    torch.cuda.synchronize()
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(reps):
+        dist.all_reduce(buf)
+    e.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([s.elapsed_time(e) / reps * 1e3], device=buf.device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def cfg5_sharded(args, dev, world, rank, dist):
+    """BASELINE config 5 strong-scaled over the ranks: B=64 T=8192 D=8192 W=8 bf16, bias + SiLU,
+    rows 64/N per GPU (shard_rows), forward + backward per step with the fp32 dweight||dbias vector
+    all-reduced over NCCL (asynchronously, double-buffered as in the headline loop). Batch row r's
+    x and dout come from generators seeded by r, so every N sees the same global batch.
+
+    After the timed steps rank 0 runs the whole batch on its one GPU and compares: the all-reduced
+    weight/bias gradient against the single-GPU one (within the bf16 sum tolerance,
+    1e-2 * max(1, max|g|)), and its own shard's out and dx against the same rows of the
+    single-GPU run (bit for bit: a row's results do not depend on the other rows)."""
+    from causal_conv1d_b200.causal_conv1d import _bwd, _fwd
+    from causal_conv1d_b200.distributed import shard_rows
+
+    B, T, D, W = 64, 8192, 8192, 8
+    rows = shard_rows(B, rank, world)
+    nb = rows.stop - rows.start
+    g = torch.Generator(device=dev)
+
+    def rows_of(r0, r1, seed):
+        t = torch.empty(r1 - r0, T, D, dtype=torch.bfloat16, device=dev)
+        for r in range(r0, r1):
+            g.manual_seed(seed + r)
+            t[r - r0].normal_(generator=g)
+        return t
+
+    g.manual_seed(5)
+    w = torch.randn(D, W, generator=g, device=dev) * W ** -0.5
+    b = torch.randn(D, generator=g, device=dev) * 0.1 ** 0.5
+    x = rows_of(rows.start, rows.stop, 1 << 20)
+    dy = rows_of(rows.start, rows.stop, 2 << 20)
+    flat = [torch.zeros(D * (W + 1), device=dev) for _ in range(2)]
+    pending = [None, None]
+    stream = torch.cuda.current_stream(dev)
+    last = {}
+
+    def step(i):
+        last["out"] = _fwd(x, w, b, None, None, None, True)
+        k = i % 2
+        if pending[k] is not None:
+            pending[k].wait()
+            pending[k] = None
+        last["dx"] = _bwd(x, w, b, None, None, dy, None, False, True, grad_f32=flat[k])[0]
+        last["k"] = k
+        if world > 1:
+            pending[k] = dist.all_reduce(flat[k], async_op=True)
+
+    def join():
+        for k in range(2):
+            if pending[k] is not None:
+                pending[k].wait()
+                pending[k] = None
+
+    warm, K = 3, args.cfg5_steps
+    for i in range(warm):
+        step(i)
+    join()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(K):
+        ev[i][0].record(stream)
+        last["out"] = None  # the previous step's output is released before the next is made
+        step(warm + i)
+        ev[i][2].record(stream)
+    join()
+    e.record(stream)
+    torch.cuda.synchronize(dev)
+    total = s.elapsed_time(e)
+    t = torch.tensor([total], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item() / K
+    step_us = sum(a[0].elapsed_time(a[2]) for a in ev) / K * 1e3
+    ar_us = allreduce_us(dist, flat[0].clone(), stream) if world > 1 else 0.0
+
+    # Single-GPU full-batch reference on rank 0.
+    res = {}
+    if rank == 0:
+        grad = flat[last["k"]]
+        if world == 1:
+            xf, dyf = x, dy
+        else:
+            xf, dyf = rows_of(0, B, 1 << 20), rows_of(0, B, 2 << 20)
+        ref = torch.zeros_like(grad)
+        outf = _fwd(xf, w, b, None, None, None, True)
+        dxf = _bwd(xf, w, b, None, None, dyf, None, False, True, grad_f32=ref)[0]
+        torch.cuda.synchronize(dev)
+        scale = max(1.0, float(ref.abs().max()))
+        diff = float((grad - ref).abs().max())
+        res = {"dweight_dbias_maxdiff_vs_1gpu": diff, "dweight_dbias_scale": scale,
+               "within_bf16_sum_tol": diff <= 1e-2 * scale,
+               "rank0_out_dx_bitexact_vs_1gpu": bool(torch.equal(outf[:nb], last["out"]) and
+                                                      torch.equal(dxf[:nb], last["dx"]))}
+        del xf, dyf, outf, dxf, ref
+    del x, dy, last
+    torch.cuda.empty_cache()
+    if dist is not None:
+        dist.barrier()
+    fb, bb = algo_bytes(B, T, D, W)
+    peak, kind = measured_peak()
+    agg = (fb + bb) / (ms * 1e-3) / 1e9
+    return {
+        "workload": "BASELINE config 5: B=64 T=8192 D=8192 W=8 bf16 bias+silu fwd+bwd, strong-scaled "
+                    "(64/N rows per GPU), NCCL all-reduce of fp32 dweight||dbias (295 KB)",
+        "rows_per_gpu": nb, "steps": K, "ms_per_step": ms, "step_us_rank_events": step_us,
+        "allreduce_us": ar_us, "agg_gbs": agg, "frac_of_measured_per_gpu": agg / (world * peak),
+        "peak": f"{kind} hbm_gbs {peak}", **res,
+    }
+
+
+def triton_arm(args, ours_line):
+    """The reference's Triton kernels on this GPU and workload (`--impl triton` in a subprocess,
+    same steps and warm-up), with the speed-ups of this repository's kernels over them."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--impl", "triton", "--gpus", "1",
+           "--steps", str(args.steps), "--warmup", str(args.warmup), "--batch", str(args.batch),
+           "--seqlen", str(args.seqlen), "--dim", str(args.dim), "--width", str(args.width)]
+    if args.no_bias_silu:
+        cmd.append("--no-bias-silu")
+    drop = {"RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE", "GROUP_RANK", "ROLE_RANK",
+            "MASTER_ADDR", "MASTER_PORT", "TORCHELASTIC_RUN_ID"}
+    env = {k: v for k, v in os.environ.items() if k not in drop}
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
+    except Exception as e:  # noqa: BLE001 - reported in the line
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"unavailable": f"rc {r.returncode}: {r.stderr.strip()[-400:]}"}
+    t = json.loads(lines[-1])
+    f_us, b_us = t["fwd"]["us_per_call"], t["bwd"]["us_per_call"]
+    return {
+        "source": "reference causal_conv1d_triton._fwd/_bwd from baseline/_ref (unmodified), same "
+                  "workload and step count, run after this arm in a subprocess",
+        "fwd_us": f_us, "bwd_us": b_us, "ms_per_step": t["ms_per_step"], "gbs": t["value"],
+        "fwd_gbs": t["fwd"]["gbs"], "bwd_gbs": t["bwd"]["gbs"], "clocks": t.get("clocks"),
+        "speedup_fwd": f_us / ours_line["fwd"]["us_per_call"],
+        "speedup_bwd": b_us / ours_line["bwd"]["us_per_call"],
+        "speedup_step": t["ms_per_step"] / ours_line["ms_per_step"],
+    }
 
 
 def e2e(args, dev, x_h, w_h, b_h, dy_h, bias_silu, world, dist):
