@@ -81,9 +81,9 @@ def _worker(rank, world, port, result_dir):
 
 
 def _paths():
-    import sys
-
-    return os.pathsep.join(p for p in sys.path if "repo" in p)
+    tests = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(tests)
+    return os.pathsep.join([tests, root, os.path.join(root, "causal-conv1d-triton_b200")])
 
 
 def test_gloo_two_ranks_match_full_batch(tmp_path):
@@ -112,3 +112,95 @@ def _failing_worker(rank, world, port):
 def test_gloo_dead_rank_raises_instead_of_hanging():
     with pytest.raises(Exception):
         mp.spawn(_failing_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _oracle_fn_class():
+    """An autograd Function that stands in for the sharded conv on the CPU: its backward computes
+    this rank's flat [dweight, dbias] with the oracle and hands it to reduce_weight_grads, the
+    same call the CUDA path makes."""
+    from causal_conv1d_b200.distributed import reduce_weight_grads
+    from oracle import oracle
+
+    class OracleShardFn(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx, x, weight, bias, seq, init, deferred):
+            ctx.save_for_backward(x, weight, bias, seq, init)
+            ctx.deferred = deferred
+            ctx.leaves = (weight, bias)
+            return torch.from_numpy(oracle.fwd(x, weight, bias, init, seq, silu=True))
+
+        @staticmethod
+        def backward(ctx, dout):
+            x, weight, bias, seq, init = ctx.saved_tensors
+            dx, dw, db, dinit = oracle.bwd(x, weight, bias, init, seq, dout, None,
+                                           need_dinit=init is not None, silu=True)
+            flat = torch.from_numpy(np.concatenate([dw.reshape(-1), db]))
+            w_leaf, b_leaf = ctx.leaves
+            gw, gb = reduce_weight_grads(flat, w_leaf, b_leaf, deferred=ctx.deferred)
+            gi = torch.from_numpy(dinit) if dinit is not None else None
+            return torch.from_numpy(dx), gw, gb, None, gi, None
+
+    return OracleShardFn
+
+
+def _varlen_inputs():
+    g = torch.Generator().manual_seed(7)
+    B, T, D, W = 5, 64, 16, 4
+    x = torch.randn(B, T, D, generator=g)
+    w = torch.randn(D, W, generator=g) * 0.5
+    b = torch.randn(D, generator=g) * 0.3
+    init = torch.randn(B, W - 1, D, generator=g)
+    seq = torch.zeros(B, T, dtype=torch.int32)
+    for r in range(B):
+        cut = int(torch.randint(8, 40, (1,), generator=g))
+        seq[r, cut:] = 1
+        seq[r, T - 3 - r:] = -1  # padding tail
+    dy = torch.randn(B, T, D, generator=g)
+    return x, w, b, init, seq, dy
+
+
+def _deferred_worker(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import sys
+
+    sys.path[:0] = [p for p in os.environ["CC1D_TEST_PATHS"].split(os.pathsep)]
+    from causal_conv1d_b200.distributed import shard_rows
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    Fn = _oracle_fn_class()
+    x, w, b, init, seq, dy = _varlen_inputs()
+    sl = shard_rows(x.shape[0], rank, world)
+    res = {}
+    for deferred in (False, True):
+        wl, bl = w.clone().requires_grad_(True), b.clone().requires_grad_(True)
+        il = init[sl].clone().requires_grad_(True)
+        out = Fn.apply(x[sl], wl, bl, seq[sl], il, deferred)
+        # A second use of the weight after the conv: its gradient must add to the reduced one.
+        loss = (out * dy[sl]).sum() + (wl * 2.0).sum()
+        loss.backward()
+        res[deferred] = (wl.grad.clone(), bl.grad.clone(), il.grad.clone())
+    torch.save(res, os.path.join(result_dir, f"d{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_gloo_deferred_reduce_equals_immediate_on_packed_shards(tmp_path):
+    """Packed variable-length rows (seq_idx with padding, initial states) sharded over 2 gloo
+    ranks: the all-reduced weight/bias gradient equals the oracle's over the whole batch, both
+    when reduced inside the backward and when deferred to the end of the backward pass."""
+    from oracle import oracle
+
+    os.environ["CC1D_TEST_PATHS"] = _paths()
+    mp.spawn(_deferred_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    r = [torch.load(tmp_path / f"d{i}.pt") for i in range(2)]
+    x, w, b, init, seq, dy = _varlen_inputs()
+    _, rdw, rdb, rdi = oracle.bwd(x, w, b, init, seq, dy, None, need_dinit=True, silu=True)
+    for rank in range(2):
+        for deferred in (False, True):
+            gw, gb, gi = r[rank][deferred]
+            np.testing.assert_allclose(gw.numpy(), rdw + 2.0, rtol=1e-5, atol=1e-5 * np.abs(rdw).max())
+            np.testing.assert_allclose(gb.numpy(), rdb, rtol=1e-5, atol=1e-5 * np.abs(rdb).max())
+        assert torch.equal(r[rank][False][0], r[rank][True][0])
+    # Each rank's dinit is its own rows' (no exchange).
+    np.testing.assert_allclose(torch.cat([r[0][True][2], r[1][True][2]]).numpy(), rdi, rtol=1e-5, atol=1e-5)
