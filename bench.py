@@ -74,7 +74,8 @@ def parse():
     ap.add_argument("--width", type=int, default=4)
     ap.add_argument("--no-bias-silu", action="store_true", help="the no-bias/no-activation mode")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline budget")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU baseline budget (0 skips the CPU baselines)")
     ap.add_argument("--cfg5-steps", type=int, default=10,
                     help="timed steps of the strong-scaled config-5 sub-record (0 skips it)")
     ap.add_argument("--no-triton-arm", action="store_true",
@@ -793,6 +794,8 @@ def main():
 
     if world > 1:
         line["allreduce_us"] = allreduce_us(dist, grad_buf[0].clone(), stream)
+    else:
+        line["host_overhead_cfg1"] = host_overhead(dev)
 
     # End to end through the public API, host buffers in and out.
     line["e2e"] = e2e(args, dev, x_h, w_h, b_h, dy_h, bias_silu, world, dist)
@@ -803,7 +806,7 @@ def main():
         line["cfg5_sharded"] = cfg5_sharded(args, dev, world, rank, dist)
 
     if rank == 0:
-        if world == 1:  # the CPU baselines and the reference's Triton arm are measured at N = 1 only
+        if world == 1 and args.cpu_seconds > 0:  # the CPU baselines are measured at N = 1 only
             threads = os.cpu_count()
             gbs, sample, _ = cpu_sample_gbs(w_h, b_h, x_h, dy_h, bias_silu, args.cpu_seconds,
                                             nthreads=threads)
@@ -813,8 +816,8 @@ def main():
                                                          args.cpu_seconds / 2)
             line["cpu_baseline_torch_conv1d"] = {"value": tg, "unit": "GB/s", "cores": os.cpu_count(),
                                                  "threads": tthreads, "sample": tsample}
-            if not args.no_triton_arm:
-                line["triton_reference"] = triton_arm(args, line)
+        if world == 1 and not args.no_triton_arm:
+            line["triton_reference"] = triton_arm(args, line)
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -949,6 +952,47 @@ def cfg5_sharded(args, dev, world, rank, dist):
         "allreduce_us": ar_us, "agg_gbs": agg, "frac_of_measured_per_gpu": agg / (world * peak),
         "peak": f"{kind} hbm_gbs {peak}", **res,
     }
+
+
+def host_overhead(dev, calls=300):
+    """Host time per eager call at BASELINE config 1 (B=2 T=1024 D=512 W=4 bf16, bias + SiLU),
+    where each kernel runs for a few microseconds and the host decides the step time: the raw
+    launchers (_fwd, _bwd: argument checks, output allocation, the C ABI call) and the whole
+    public-API step (causal_conv1d_fn + autograd backward). CPU wall time over `calls` calls,
+    median of 5 repeats, device synchronised around each repeat."""
+    from causal_conv1d_b200 import causal_conv1d_fn
+    from causal_conv1d_b200.causal_conv1d import _bwd, _fwd
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    B, T, D, W = 2, 1024, 512, 4
+    x = torch.randn(B, T, D, generator=g, device=dev, dtype=torch.bfloat16)
+    w = torch.randn(D, W, generator=g, device=dev)
+    b = torch.randn(D, generator=g, device=dev)
+    dy = torch.randn(B, T, D, generator=g, device=dev, dtype=torch.bfloat16)
+    xl, wl, bl = x.clone().requires_grad_(True), w.clone().requires_grad_(True), b.clone().requires_grad_(True)
+
+    def step():
+        xl.grad = wl.grad = bl.grad = None
+        causal_conv1d_fn(xl, wl, bl, activation="silu").backward(dy)
+
+    fns = {"fwd_launcher_us": lambda: _fwd(x, w, b, None, None, None, True),
+           "bwd_launcher_us": lambda: _bwd(x, w, b, None, None, dy, None, False, True),
+           "autograd_step_us": step}
+    out = {}
+    for name, fn in fns.items():
+        for _ in range(20):
+            fn()
+        reps = []
+        for _ in range(5):
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            for _ in range(calls):
+                fn()
+            reps.append((time.perf_counter() - t0) / calls * 1e6)
+            torch.cuda.synchronize(dev)
+        out[name] = statistics.median(reps)
+    out["workload"] = "BASELINE config 1: B=2 T=1024 D=512 W=4 bf16 bias+silu, eager, CPU wall time per call"
+    return out
 
 
 def triton_arm(args, ours_line):

@@ -1,5 +1,7 @@
 """Builds libcausal_conv1d_b200.so (the C-ABI library of include/causal_conv1d_b200.h) for
-sm_100a with nvcc, in-tree: objects under _build/, the library inside the Python package.
+sm_100a with nvcc, in-tree: objects under _build/, the library inside the Python package; then the
+package's CPython binding of the hot entry points (csrc/cc1d_pyfast.c -> _cc1d_fast*.so), linked
+against that library.
 
     python causal-conv1d-triton_b200/build.py [--force] [--verbose]
 """
@@ -12,6 +14,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
@@ -19,6 +22,8 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "causal_conv1d_b200", "libcausal_conv1d_b200.so")
+FAST_SRC = os.path.join(CSRC, "cc1d_pyfast.c")
+FAST = os.path.join(HERE, "causal_conv1d_b200", "_cc1d_fast" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
@@ -80,13 +85,32 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
                 if ptxas_verbose and err:
                     print(f"== {os.path.basename(s)}\n{err}", flush=True)
     if force or todo or _stale(lib_path, objs):
-        cmd = [nvcc] + ARCH + ["-shared", "-o", lib_path] + objs
+        cmd = [nvcc] + ARCH + ["-shared", "-Xlinker", "-soname=libcausal_conv1d_b200.so", "-o", lib_path] + objs
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    if lib_path == LIB:
+        build_fast(force, verbose)
     return lib_path
+
+
+def build_fast(force: bool = False, verbose: bool = False) -> str:
+    """Compiles the CPython binding (C, no CUDA code) against the built library."""
+    header = os.path.join(INCLUDE, "causal_conv1d_b200.h")
+    if not (force or _stale(FAST, [FAST_SRC, header, LIB])):
+        return FAST
+    cc = shutil.which("gcc") or "cc"
+    cmd = [cc, "-O2", "-fPIC", "-shared", "-std=c11", "-Wall", "-Wextra",
+           "-I", sysconfig.get_paths()["include"], "-I", INCLUDE, FAST_SRC,
+           "-L", os.path.dirname(LIB), "-lcausal_conv1d_b200", "-Wl,-rpath,$ORIGIN", "-o", FAST]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"binding build failed:\n{r.stdout}\n{r.stderr}")
+    return FAST
 
 
 if __name__ == "__main__":

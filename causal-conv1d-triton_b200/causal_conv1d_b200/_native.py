@@ -1,7 +1,10 @@
-"""ctypes binding of libcausal_conv1d_b200.so, the C ABI declared in include/causal_conv1d_b200.h.
+"""Bindings of libcausal_conv1d_b200.so, the C ABI declared in include/causal_conv1d_b200.h.
 
-The library is built in-tree by causal-conv1d-triton_b200/build.py. Importing this module without
-it raises ImportError: there is no CPU or Python fallback for the kernels.
+`lib` binds every entry point with ctypes. `fast` is the package's CPython binding of the hot
+launch entry points (cc1d_fwd, cc1d_bwd_workspace_bytes, cc1d_bwd, cc1d_update; built from
+csrc/cc1d_pyfast.c), which parses arguments in a fraction of ctypes' per-call time; both reach
+the same loaded library. Both are built in-tree by causal-conv1d-triton_b200/build.py. Importing
+this module without them raises ImportError: there is no CPU or Python fallback for the kernels.
 """
 
 from __future__ import annotations
@@ -75,6 +78,12 @@ def _load():
 
 
 lib = _load()
+
+try:
+    from . import _cc1d_fast as fast  # noqa: E402  (links libcausal_conv1d_b200.so, loaded above)
+except ImportError as e:  # pragma: no cover - only without a build
+    raise ImportError(f"the package's CPython binding is missing ({e}): build the CUDA library first "
+                      "(python causal-conv1d-triton_b200/build.py)") from e
 
 
 class CausalConv1dError(RuntimeError):

@@ -19,7 +19,7 @@ import torch
 from torch import Tensor
 
 from . import _native
-from ._native import DTYPE_CODE, check, lib
+from ._native import DTYPE_CODE, check, fast, lib
 
 _FLOAT = (torch.float32, torch.float16, torch.bfloat16)
 
@@ -119,25 +119,46 @@ def _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu):
     out = torch.empty(B, T, D, device=x.device, dtype=x.dtype)
     w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
     with _DeviceGuard(x.device):
-        check(
-            lib.cc1d_fwd(
-                x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
-                _ptr(seq_idx), out.data_ptr(), _ptr(final_states), B, T, D, W,
-                DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
-                _stream(x.device),
-            ),
-            "causal_conv1d forward",
+        rc = fast.fwd(
+            x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
+            _ptr(seq_idx), out.data_ptr(), _ptr(final_states), B, T, D, W,
+            DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
+            _stream(x.device),
         )
+    if rc:
+        check(rc, "causal_conv1d forward")
     return out
 
 
+# Workspace bytes of the backward by (device, dtype, sizes, strides, 16-byte alignment of x and
+# dout): the library's plan is a pure function of these, so a step need not re-plan through the
+# library to size its workspace.
+_WS_CACHE: dict = {}
+
+
+def _workspace_bytes(x, dout, B, T, D, W):
+    key = (x.device.index, x.dtype, B, T, D, W, x.stride(0), x.stride(1), dout.stride(0), dout.stride(1),
+           x.data_ptr() % 16, dout.data_ptr() % 16)
+    n = _WS_CACHE.get(key)
+    if n is None:
+        n = fast.bwd_workspace_bytes(x.data_ptr(), x.stride(0), x.stride(1), dout.data_ptr(),
+                                     dout.stride(0), dout.stride(1), B, T, D, W, DTYPE_CODE[x.dtype])
+        if n < 0:
+            check(_native.CC1D_ERR_INVALID, "causal_conv1d backward workspace")
+        if len(_WS_CACHE) > 4096:
+            _WS_CACHE.clear()
+        _WS_CACHE[key] = n
+    return n
+
+
 def _bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_dinit, silu,
-         grad_f32=None):
+         grad_f32=None, fuse_param_grads=True):
     """Host launcher of the backward (the reference's `_bwd`, causal_conv1d.py:475-541).
 
     Returns (dx, dweight, dbias, dinit). With `grad_f32` (a contiguous fp32 tensor of D * (W + 1)
     elements) the weight/bias gradients are written there as [dweight (D, W), dbias (D)] instead,
-    and dweight/dbias are returned as None.
+    and dweight/dbias are returned as None. With fp32 weight and bias and `fuse_param_grads`,
+    dweight and dbias are views of one fp32 buffer (one allocation fewer per call).
     """
     B, T, D = x.shape
     W = weight.shape[1]
@@ -145,35 +166,39 @@ def _bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_din
     dinit = torch.empty_like(initial_states) if need_dinit else None
     w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
     dinit_k = _as_float(dinit)
+    flat = None
     if grad_f32 is None:
-        dweight = torch.empty_like(w)
-        dbias = torch.empty_like(b) if b is not None else None
+        if fuse_param_grads and weight.dtype == torch.float32 and (bias is None or bias.dtype == torch.float32):
+            # fp32 parameters: one allocation holds [dweight (D, W), dbias (D)], written by the
+            # kernel's fp32 gradient output; the gradients are views of it.
+            flat = torch.empty(D * (W + 1), device=x.device, dtype=torch.float32)
+            dweight, dbias = None, None
+        else:
+            dweight = torch.empty_like(w)
+            dbias = torch.empty_like(b) if b is not None else None
     else:
         dweight = dbias = None
     if dfinal_states is not None and dfinal_states.dtype != x.dtype:
         dfinal_states = dfinal_states.to(x.dtype)
     with _DeviceGuard(x.device):
-        ws_bytes = lib.cc1d_bwd_workspace_bytes(
-            x.data_ptr(), x.stride(0), x.stride(1), dout.data_ptr(), dout.stride(0),
-            dout.stride(1), B, T, D, W, DTYPE_CODE[x.dtype],
-        )
-        if ws_bytes < 0:
-            check(_native.CC1D_ERR_INVALID, "causal_conv1d backward workspace")
+        ws_bytes = _workspace_bytes(x, dout, B, T, D, W)
         workspace = torch.empty(max(1, ws_bytes // 4), device=x.device, dtype=torch.float32)
-        check(
-            lib.cc1d_bwd(
-                x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
-                _ptr(seq_idx), dout.data_ptr(), dout.stride(0), dout.stride(1),
-                _ptr(dfinal_states), dx.data_ptr(), _ptr(dweight), _ptr(dbias), _ptr(dinit_k),
-                _ptr(grad_f32), workspace.data_ptr(), ws_bytes, B, T, D, W,
-                DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
-                _stream(x.device),
-            ),
-            "causal_conv1d backward",
+        rc = fast.bwd(
+            x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
+            _ptr(seq_idx), dout.data_ptr(), dout.stride(0), dout.stride(1),
+            _ptr(dfinal_states), dx.data_ptr(), _ptr(dweight), _ptr(dbias), _ptr(dinit_k),
+            _ptr(grad_f32 if grad_f32 is not None else flat), workspace.data_ptr(), ws_bytes, B, T, D, W,
+            DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
+            _stream(x.device),
         )
+    if rc:
+        check(rc, "causal_conv1d backward")
     if dinit is not None and dinit_k is not dinit:
         dinit.copy_(dinit_k)
-    if grad_f32 is None:
+    if flat is not None:
+        dweight = flat[: D * W].view(D, W)
+        dbias = flat[D * W:] if bias is not None else None
+    elif grad_f32 is None:
         if dweight.dtype != weight.dtype:
             dweight = dweight.to(weight.dtype)
         if dbias is not None and dbias.dtype != bias.dtype:
@@ -391,15 +416,14 @@ def causal_conv1d_update(
     w, b = _as_float(weight.contiguous()), _as_float(bias.contiguous() if bias is not None else None)
     out = torch.empty(B, L, D, device=x.device, dtype=x.dtype)
     with _DeviceGuard(x.device):
-        check(
-            lib.cc1d_update(
-                x.data_ptr(), x.stride(0), x.stride(1), conv_state.data_ptr(),
-                _ptr(conv_state_indices), w.data_ptr(), _ptr(b), out.data_ptr(), B, L, D, W,
-                DTYPE_CODE[x.dtype], DTYPE_CODE[conv_state.dtype], DTYPE_CODE[w.dtype], _code(b),
-                int(activation is not None), _stream(x.device),
-            ),
-            "causal_conv1d update",
+        rc = fast.update(
+            x.data_ptr(), x.stride(0), x.stride(1), conv_state.data_ptr(),
+            _ptr(conv_state_indices), w.data_ptr(), _ptr(b), out.data_ptr(), B, L, D, W,
+            DTYPE_CODE[x.dtype], DTYPE_CODE[conv_state.dtype], DTYPE_CODE[w.dtype], _code(b),
+            int(activation is not None), _stream(x.device),
         )
+    if rc:
+        check(rc, "causal_conv1d update")
     return out.squeeze(1) if squeeze else out
 
 

@@ -42,8 +42,10 @@ def _(x, weight, bias, seq_idx, initial_states, return_final_states, silu):
 def bwd_op(x: Tensor, weight: Tensor, bias: Tensor | None, seq_idx: Tensor | None,
            initial_states: Tensor | None, dout: Tensor, dfinal_states: Tensor | None,
            need_dinit: bool, silu: bool) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    # Outputs of a custom op may not alias one another: separate weight / bias gradient buffers.
     dx, dweight, dbias, dinit = _bwd(x, weight, bias, seq_idx, initial_states,
-                                     _channels_contiguous(dout), dfinal_states, need_dinit, silu)
+                                     _channels_contiguous(dout), dfinal_states, need_dinit, silu,
+                                     fuse_param_grads=False)
     return (dx, dweight, dbias if dbias is not None else x.new_empty(0),
             dinit if dinit is not None else x.new_empty(0))
 

@@ -156,3 +156,30 @@ def test_tma_layout_routing():
     assert copied.data_ptr() != leaf.data_ptr()
     copied.float().sum().backward()  # the copy is differentiable
     assert (leaf.grad[..., 1:] == 1).all() and (leaf.grad[..., 0] == 0).all()
+
+
+def test_fast_binding_checks_arguments_and_returns_abi_codes():
+    """The package's CPython binding of the hot entry points (csrc/cc1d_pyfast.c) loads without a
+    GPU, rejects a wrong argument count or type with a Python error, and returns the C ABI's own
+    codes: an invalid dtype code or width is refused before any CUDA call."""
+    from causal_conv1d_b200 import _native
+
+    fast = _native.fast
+    fwd = [1, 2, 3, 4, None, None, None, 5, None, 1, 2, 3, 4, 9, 0, 0, 0, 1, 0]
+    assert fast.fwd(*fwd) == _native.CC1D_ERR_INVALID  # dtype code 9
+    assert _native.lib.cc1d_fwd(*fwd) == _native.CC1D_ERR_INVALID
+    bwd = [1, 2, 3, 4, None, None, None, 5, 6, 7, None, 8, 9, None, None, None, 10, 11,
+           1, 2, 3, 4, 9, 0, 0, 0, 1, 0]
+    assert fast.bwd(*bwd) == _native.CC1D_ERR_INVALID
+    bwd_w = list(bwd)
+    bwd_w[21], bwd_w[22] = 300, 2  # width 300 > 256, bf16
+    assert fast.bwd(*bwd_w) == _native.lib.cc1d_bwd(*bwd_w) == _native.CC1D_ERR_UNSUPPORTED
+    assert fast.bwd_workspace_bytes(1, 2, 3, 4, 5, 6, 1, 2, 3, 1, 2) == -1  # width 1
+    upd = [1, 2, 3, 4, None, 5, None, 6, 1, 1, 3, 4, 9, 0, 0, 0, 1, 0]
+    assert fast.update(*upd) == _native.CC1D_ERR_INVALID
+    with pytest.raises(TypeError):
+        fast.fwd(*fwd[:-1])
+    with pytest.raises(TypeError):
+        fast.bwd(*bwd, 0)
+    with pytest.raises(TypeError):
+        fast.fwd(*(["x"] + fwd[1:]))
