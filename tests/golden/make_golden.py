@@ -12,7 +12,7 @@ Two things the reference needs a GPU for are replaced, as the interpreter cannot
 itself asserts `x.is_cuda` (causal_conv1d.py:403), so the public API's argument handling
 (causal_conv1d.py:605-634, 544-576) is restated in `run_case` around the two launchers.
 
-Usage: python tests/golden/make_golden.py [--ref /path/to/causal-conv1d-triton]
+Usage: python tests/golden/make_golden.py --ref /path/to/causal-conv1d-triton
 """
 
 from __future__ import annotations
@@ -111,7 +111,9 @@ def run_case(cc, i, spec):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True,
+                    help="checkout of jxiong21029/causal-conv1d-triton (the directory holding the "
+                         "causal_conv1d_triton package)")
     args = ap.parse_args()
     cc = load_reference(args.ref)
     arrays, metas = {}, []

@@ -3,7 +3,10 @@
 split_conv1d(zxbcdt, ...) must equal the unfused composition
     z, xBC, dt = zxbcdt.split(...); parts = causal_conv1d_fn(xBC, ...).split(...)
 in every output and every gradient, bit for bit: the same kernels compute the same elements; the
-fused backward only reads the parts' gradients where they lie and writes dxBC into d(zxbcdt).
+fused backward only reads the parts' gradients where they lie and writes dxBC into d(zxbcdt). The
+fused results are also checked against the CPU oracle: the conv outputs and the xBC slice of
+d(zxbcdt), dweight, dbias and dinit within the parity tolerance, the z and dt slices of d(zxbcdt)
+equal to their upstream gradients.
 Cases cover the TMA split path (piece boundaries on 128- or 64-channel blocks), seq_idx with
 initial states, W = 8, fp32, and layouts outside the fast path (misaligned pieces, a row stride
 that is not a 16-byte multiple), which fall back to concatenating. A direct C-ABI call checks that
@@ -77,6 +80,25 @@ def test_split_conv1d_equals_unfused(case):
         assert torch.equal(a, c), f"output {i} differs"
     for i, (a, c) in enumerate(zip(gf, gu)):
         assert torch.equal(a, c), f"gradient {i} differs"
+
+    # Against the oracle, on the conv's own input slice.
+    from _tol import assert_close, assert_close_sum
+    from oracle import oracle
+
+    key = "f32" if dt == torch.float32 else "bf16"
+    xbc = zx[..., d_z:d_z + d_xbc]
+    ups = upstream[1:1 + len(split)]
+    eo = oracle.fwd(xbc, w, b, init, seq_idx, silu=silu)
+    assert_close(torch.cat(of[1:1 + len(split)], -1), eo, key, "conv output vs oracle")
+    edx, edw, edb, edi = oracle.bwd(xbc, w, b, init, seq_idx, torch.cat(ups, -1), None,
+                                    need_dinit=init is not None, silu=silu)
+    dzx = gf[0]
+    assert_close(dzx[..., d_z:d_z + d_xbc], edx, key, "dxBC vs oracle")
+    assert torch.equal(dzx[..., :d_z], upstream[0]) and torch.equal(dzx[..., d_z + d_xbc:], upstream[-1])
+    assert_close_sum(gf[1], edw, key, "dweight vs oracle")
+    assert_close_sum(gf[2], edb, key, "dbias vs oracle")
+    if init is not None:
+        assert_close(gf[3], edi, key, "dinit vs oracle")
     from causal_conv1d_b200 import _native
 
     assert _native.status(clear=True) == 0
