@@ -116,14 +116,15 @@ def _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu):
         raise TypeError(f"x must be float32, float16 or bfloat16, got {x.dtype}")
     B, T, D = x.shape
     W = weight.shape[1]
-    out = torch.empty(B, T, D, device=x.device, dtype=x.dtype)
+    dev = x.device
+    out = torch.empty(B, T, D, device=dev, dtype=x.dtype)
     w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
-    with _DeviceGuard(x.device):
+    with _DeviceGuard(dev):
         rc = fast.fwd(
             x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
             _ptr(seq_idx), out.data_ptr(), _ptr(final_states), B, T, D, W,
             DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
-            _stream(x.device),
+            _stream(dev),
         )
     if rc:
         check(rc, "causal_conv1d forward")
@@ -136,8 +137,8 @@ def _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu):
 _WS_CACHE: dict = {}
 
 
-def _workspace_bytes(x, dout, B, T, D, W):
-    key = (x.device.index, x.dtype, B, T, D, W, x.stride(0), x.stride(1), dout.stride(0), dout.stride(1),
+def _workspace_bytes(x, dout, B, T, D, W, dev_index):
+    key = (dev_index, x.dtype, B, T, D, W, x.stride(0), x.stride(1), dout.stride(0), dout.stride(1),
            x.data_ptr() % 16, dout.data_ptr() % 16)
     n = _WS_CACHE.get(key)
     if n is None:
@@ -162,7 +163,8 @@ def _bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_din
     """
     B, T, D = x.shape
     W = weight.shape[1]
-    dx = torch.empty(B, T, D, device=x.device, dtype=x.dtype)
+    dev = x.device
+    dx = torch.empty(B, T, D, device=dev, dtype=x.dtype)
     dinit = torch.empty_like(initial_states) if need_dinit else None
     w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
     dinit_k = _as_float(dinit)
@@ -171,7 +173,7 @@ def _bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_din
         if fuse_param_grads and weight.dtype == torch.float32 and (bias is None or bias.dtype == torch.float32):
             # fp32 parameters: one allocation holds [dweight (D, W), dbias (D)], written by the
             # kernel's fp32 gradient output; the gradients are views of it.
-            flat = torch.empty(D * (W + 1), device=x.device, dtype=torch.float32)
+            flat = torch.empty(D * (W + 1), device=dev, dtype=torch.float32)
             dweight, dbias = None, None
         else:
             dweight = torch.empty_like(w)
@@ -180,24 +182,27 @@ def _bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_din
         dweight = dbias = None
     if dfinal_states is not None and dfinal_states.dtype != x.dtype:
         dfinal_states = dfinal_states.to(x.dtype)
-    with _DeviceGuard(x.device):
-        ws_bytes = _workspace_bytes(x, dout, B, T, D, W)
-        workspace = torch.empty(max(1, ws_bytes // 4), device=x.device, dtype=torch.float32)
+    with _DeviceGuard(dev):
+        ws_bytes = _workspace_bytes(x, dout, B, T, D, W, dev.index)
+        workspace = torch.empty(max(1, ws_bytes // 4), device=dev, dtype=torch.float32)
         rc = fast.bwd(
             x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
             _ptr(seq_idx), dout.data_ptr(), dout.stride(0), dout.stride(1),
             _ptr(dfinal_states), dx.data_ptr(), _ptr(dweight), _ptr(dbias), _ptr(dinit_k),
             _ptr(grad_f32 if grad_f32 is not None else flat), workspace.data_ptr(), ws_bytes, B, T, D, W,
             DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
-            _stream(x.device),
+            _stream(dev),
         )
     if rc:
         check(rc, "causal_conv1d backward")
     if dinit is not None and dinit_k is not dinit:
         dinit.copy_(dinit_k)
     if flat is not None:
-        dweight = flat[: D * W].view(D, W)
-        dbias = flat[D * W:] if bias is not None else None
+        if bias is not None:
+            dweight, dbias = flat.split((D * W, D))
+            dweight = dweight.view(D, W)
+        else:
+            dweight = flat[: D * W].view(D, W)
     elif grad_f32 is None:
         if dweight.dtype != weight.dtype:
             dweight = dweight.to(weight.dtype)

@@ -138,8 +138,8 @@ bool tma_layout_ok(const void* ptr, int64_t sb, int64_t st, int64_t B, int64_t D
 
 // 3-D tensor map over a (B, T, D) channels-last tensor, as dims (D, T, B), box (box_d, box_t, 1).
 // Rows outside [0, T) and channels outside [0, D) read as zero.
-bool encode_3d(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t T, int64_t D, int64_t sb,
-               int64_t st, int box_d, int box_t) {
+bool encode_3d_uncached(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t T, int64_t D, int64_t sb,
+                        int64_t st, int box_d, int box_t) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
   if (tensor_map_encoder(&enc) != CC1D_OK) return false;
   const int es = elem_size(dtype);
@@ -155,6 +155,49 @@ bool encode_3d(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t
                          CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// The encoded maps of recent calls, keyed by every argument of the encoding (the map is a pure
+// function of them): a training loop passes the same buffers step after step, and re-encoding
+// two or three maps per call is a measurable share of a small call's host time.
+struct MapKey {
+  const void* base;
+  int64_t B, T, D, sb, st;
+  int dtype, box_d, box_t;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && B == o.B && T == o.T && D == o.D && sb == o.sb && st == o.st && dtype == o.dtype &&
+           box_d == o.box_d && box_t == o.box_t;
+  }
+};
+constexpr int kMapCache = 64;
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool used = false;
+};
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+
+bool encode_3d(CUtensorMap* map, const void* base, int dtype, int64_t B, int64_t T, int64_t D, int64_t sb,
+               int64_t st, int box_d, int box_t) {
+  const MapKey key{base, B, T, D, sb, st, dtype, box_d, box_t};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (const MapEntry& e : g_maps) {
+      if (e.used && e.key == key) {
+        *map = e.map;
+        return true;
+      }
+    }
+  }
+  if (!encode_3d_uncached(map, base, dtype, B, T, D, sb, st, box_d, box_t)) return false;
+  std::lock_guard<std::mutex> lk(g_mu);
+  MapEntry& e = g_maps[g_map_next];
+  g_map_next = (g_map_next + 1) % kMapCache;
+  e.key = key;
+  e.map = *map;
+  e.used = true;
+  return true;
 }
 
 // Template width of the TMA kernels for a true width W, or 0 for the generic path. Widths 9..16
@@ -218,8 +261,9 @@ struct BwdPlan {
   int64_t ws_bytes = 0;
 };
 
-int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t syb, int64_t syt, int64_t B, int64_t T,
-             int64_t D, int64_t W, int x_dtype, bool seq, bool silu, const DeviceInfo& di, int dev, BwdPlan* pl) {
+int plan_bwd_uncached(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t syb, int64_t syt, int64_t B,
+                      int64_t T, int64_t D, int64_t W, int x_dtype, bool seq, bool silu, const DeviceInfo& di, int dev,
+                      BwdPlan* pl) {
   const int es = elem_size(x_dtype);
   pl->wt = tma_width(W);
   pl->tma = pl->wt > 0 && tma_layout_ok(x, sxb, sxt, B, D, es) && tma_layout_ok(dy, syb, syt, B, D, es);
@@ -265,6 +309,42 @@ int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t sy
   pl->grid = static_cast<int64_t>(pl->P) * pl->n_blk;
   if (pl->grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
   pl->ws_bytes = static_cast<int64_t>(pl->P) * (W + 1) * D * 4;
+  return CC1D_OK;
+}
+
+// The plan depends on the sizes, the element type, the device, the kernel variant (seq_idx,
+// activation) and on which layouts x and dout have (TMA, cp.async chunks, or neither), not on
+// the addresses themselves: plans are cached by exactly those.
+struct PlanKey {
+  int64_t B, T, D, W;
+  int x_dtype, dev, layout;
+  bool seq, silu;
+  bool operator<(const PlanKey& o) const {
+    return std::tie(B, T, D, W, x_dtype, dev, layout, seq, silu) <
+           std::tie(o.B, o.T, o.D, o.W, o.x_dtype, o.dev, o.layout, o.seq, o.silu);
+  }
+};
+std::map<PlanKey, BwdPlan> g_plans;
+
+int plan_bwd(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t syb, int64_t syt, int64_t B, int64_t T,
+             int64_t D, int64_t W, int x_dtype, bool seq, bool silu, const DeviceInfo& di, int dev, BwdPlan* pl) {
+  const int es = elem_size(x_dtype);
+  const int layout = (tma_layout_ok(x, sxb, sxt, B, D, es) && tma_layout_ok(dy, syb, syt, B, D, es))       ? 2
+                     : (chunk_layout_ok(x, sxb, sxt, B, D, es) && chunk_layout_ok(dy, syb, syt, B, D, es)) ? 1
+                                                                                                            : 0;
+  const PlanKey key{B, T, D, W, x_dtype, dev, layout, seq, silu};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_plans.find(key);
+    if (it != g_plans.end()) {
+      *pl = it->second;
+      return CC1D_OK;
+    }
+  }
+  CC1D_TRY(plan_bwd_uncached(x, sxb, sxt, dy, syb, syt, B, T, D, W, x_dtype, seq, silu, di, dev, pl));
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_plans.size() > 4096) g_plans.clear();
+  g_plans[key] = *pl;
   return CC1D_OK;
 }
 
