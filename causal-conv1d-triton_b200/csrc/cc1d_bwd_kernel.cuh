@@ -133,8 +133,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
   constexpr int XDT = sizeof(T) == 4 ? kF32 : (std::is_same_v<T, __nv_bfloat16> ? kBF16 : kF16);
 
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + (kSmemAlign - 1)) & ~uintptr_t(kSmemAlign - 1));
+  unsigned char* smem = aligned_smem<kSmemAlign>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + S;
   unsigned char* stage0 = smem + kBarBytes;

@@ -37,6 +37,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The first ALIGN-aligned byte of a dynamic shared-memory array, as an offset from the array
+// itself: rounding the address up through an integer would hide from the compiler that the
+// result points into shared memory, and the loads and stores through it would be issued as
+// generic accesses instead of shared-memory ones.
+template <int ALIGN>
+__device__ __forceinline__ unsigned char* aligned_smem(unsigned char* raw) {
+  const uint32_t a = smem_u32(raw);
+  return raw + (((a + (ALIGN - 1)) & ~uint32_t(ALIGN - 1)) - a);
+}
+
 __device__ __forceinline__ unsigned long long global_timer_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -222,8 +222,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   constexpr bool FAST = sizeof(T) == 2;
 
   extern __shared__ unsigned char smem_raw[];
-  unsigned char* smem = reinterpret_cast<unsigned char*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + (kSmemAlign - 1)) & ~uintptr_t(kSmemAlign - 1));
+  unsigned char* smem = aligned_smem<kSmemAlign>(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   unsigned char* tile = smem + kBarBytes;
 
