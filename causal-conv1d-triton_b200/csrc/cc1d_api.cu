@@ -271,41 +271,56 @@ int plan_bwd_uncached(const void* x, int64_t sxb, int64_t sxt, const void* dy, i
     pl->tma = true;
     pl->plain = true;
   }
-  int occ = 0;
+  const int64_t rows = B * T;
   if (pl->tma) {
-    pl->k = bwd_tma_for(x_dtype, pl->wt, seq, silu, pl->plain);
-    pl->max_smem = pl->k.smem;
-    // The partial count must not depend on seq_idx or the activation (the workspace query sees
-    // neither): size the grid by the lowest occupancy of the four variants, all of which cover the
-    // same channels per CTA.
-    occ = 1 << 30;
+    // One resident wave per launch: P CTAs per channel group, each walking an equal stretch of the
+    // B*T rows (a multiple of the stage height). The variants with and without seq_idx and SiLU
+    // may differ in CTA width and occupancy (the SiLU kernels of widths 5..8 are warp-specialized,
+    // one CTA of 1024 channels per SM); the workspace query sees neither flag, so the workspace is
+    // sized for the largest partial count of the four, and each launch uses its own.
+    int64_t p_max = 1;
     for (int v = 0; v < 4; ++v) {
-      const KernelInfo kv = bwd_tma_for(x_dtype, pl->wt, (v & 1) != 0, (v & 2) != 0, pl->plain);
-      if (kv.d_tile != pl->k.d_tile) return CC1D_ERR_INVALID;
+      const bool vseq = (v & 1) != 0, vsilu = (v & 2) != 0;
+      const KernelInfo kv = bwd_tma_for(x_dtype, pl->wt, vseq, vsilu, pl->plain);
+      if (kv.fn == nullptr) return CC1D_ERR_INVALID;
+      if (kv.min_regs > 0) {
+        // A warp-specialized kernel moves registers between its warpgroups with setmaxnreg; the
+        // increase waits until the registers exist, so the launch must hold the whole split.
+        cudaFuncAttributes fa{};
+        CC1D_TRY_CUDA(cudaFuncGetAttributes(&fa, kv.fn));
+        if (fa.numRegs < kv.min_regs) return CC1D_ERR_UNSUPPORTED;
+      }
       int o = 0;
       CC1D_TRY(occupancy(kv, kv.smem, dev, &o));
-      occ = std::min(occ, o);
+      const int64_t n_blk = cdiv(D, kv.d_tile);
+      const int64_t rs = kv.t_tile;
+      const int64_t cap = static_cast<int64_t>(di.sms) * o;
+      const int64_t pw = std::max<int64_t>(1, std::min<int64_t>(cdiv(rows, rs), cap / n_blk));
+      const int64_t rpp = cdiv(cdiv(rows, pw), rs) * rs;
+      const int64_t P = cdiv(rows, rpp);
+      p_max = std::max(p_max, P);
+      if (vseq == seq && vsilu == silu) {
+        pl->k = kv;
+        pl->max_smem = kv.smem;
+        pl->n_blk = static_cast<int>(n_blk);
+        pl->rows_per_part = rpp;
+        pl->P = static_cast<int>(P);
+      }
     }
-  } else {
-    pl->k = bwd_generic_for(x_dtype, static_cast<int>(W));
-    pl->max_smem = generic_bwd_smem(kGenericMaxWidth);
-    CC1D_TRY(occupancy(pl->k, pl->max_smem, dev, &occ));
+    pl->grid = static_cast<int64_t>(pl->P) * pl->n_blk;
+    if (pl->grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+    pl->ws_bytes = p_max * (W + 1) * D * 4;
+    return CC1D_OK;
   }
+  int occ = 0;
+  pl->k = bwd_generic_for(x_dtype, static_cast<int>(W));
+  pl->max_smem = generic_bwd_smem(kGenericMaxWidth);
+  CC1D_TRY(occupancy(pl->k, pl->max_smem, dev, &occ));
   pl->n_blk = static_cast<int>(cdiv(D, pl->k.d_tile));
   const int64_t cap = static_cast<int64_t>(di.sms) * occ;
-  if (pl->tma) {
-    // One resident wave: P CTAs per channel group, each walking an equal stretch of the B*T rows
-    // (a multiple of the stage height).
-    const int64_t rows = B * T;
-    const int64_t rs = pl->k.t_tile;
-    const int64_t pmax = std::max<int64_t>(1, std::min<int64_t>(cdiv(rows, rs), cap / pl->n_blk));
-    pl->rows_per_part = cdiv(cdiv(rows, pmax), rs) * rs;
-    pl->P = static_cast<int>(cdiv(rows, pl->rows_per_part));
-  } else {
-    pl->n_tt = static_cast<int>(cdiv(T, pl->k.t_tile));
-    const int64_t M = B * pl->n_tt;
-    pl->P = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(M, cap / pl->n_blk)));
-  }
+  pl->n_tt = static_cast<int>(cdiv(T, pl->k.t_tile));
+  const int64_t M = B * pl->n_tt;
+  pl->P = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(M, cap / pl->n_blk)));
   pl->grid = static_cast<int64_t>(pl->P) * pl->n_blk;
   if (pl->grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
   pl->ws_bytes = static_cast<int64_t>(pl->P) * (W + 1) * D * 4;

@@ -16,7 +16,10 @@
 //
 // Each CTA runs one producer warp, which issues per stage one TMA load of x (rows a_lo-(W-1) ..
 // a_lo+15) and one of dout (rows a_lo .. a_lo+15) per channel block into a 2-stage mbarrier ring
-// and writes the stage's seq_idx window, and the consumer warps. Stages are aligned to the bottom of each segment, so the
+// and writes the stage's seq_idx window, and the consumer warps. With SiLU at template widths
+// 5..8 the CTA is warp-specialized: warpgroup 0 (whose warp 0 is the producer) gives up its
+// registers with setmaxnreg and two consumer warpgroups (8 channel blocks) take them, 232 per
+// thread instead of 168, one CTA per SM. Stages are aligned to the bottom of each segment, so the
 // last stage of a segment starts exactly at its first row; only the segment's top stage can be
 // partial. Consumer lanes own CPT consecutive channels (a 4- or 8-byte vector) and compute in fp32 pairs
 // with the sm_100 f32x2 instructions. A stage whose 16 rows all belong to the segment (no halo, no
@@ -42,7 +45,17 @@ constexpr int kMaxDoutPieces = 4;
 // latency and runs best with 8-byte lanes (4 channels of bf16) and 4 warps per CTA; without it the
 // kernel is bandwidth-bound and 4-byte lanes with 8 warps per CTA keep more rows in flight (both
 // measured on B200 at BASELINE config 2).
-template <typename T, int W, bool SILU>
+// Warp-specialized walk for SiLU at template widths 5..8 on the TMA path: 1 (the default): one
+// CTA per SM of a producer warpgroup and two consumer warpgroups; 2: two CTAs per SM of a
+// producer warpgroup and one consumer warpgroup; 0: the 5-warp walk. The producer warpgroup gives
+// its registers to the consumers with setmaxnreg (see BwdCfg). Measured on B200 at B=16 T=8192
+// D=8192 W=8 bf16 with SiLU: 1530 / 1635 / 1866 us for 1 / 2 / 0 (without SiLU, where the walk is
+// bound by its data movement, layout 1 is 5 % slower and 2 equal to 0).
+#ifndef CC1D_BWD_WS
+#define CC1D_BWD_WS 1
+#endif
+
+template <typename T, int W, bool SILU, bool PLAIN = false>
 struct BwdCfg {
   static constexpr int ES = static_cast<int>(sizeof(T));
   // bytes per lane: 8 with SiLU, above W = 4 and for fp32; 4 without SiLU up to W = 4 and for
@@ -52,8 +65,20 @@ struct BwdCfg {
   static constexpr int D_TILE = ROW_BYTES / ES;  // channels per warp
   static constexpr int CPT = VEC / ES;           // channels per lane
   static constexpr int NP = CPT / 2;             // fp32 pairs per lane
-  static constexpr int WARPS = (VEC == 8 || W > 8) ? 4 : 8;  // consumer warps = channel blocks per CTA
-  static constexpr int THREADS = WARPS * 32 + 32;
+  // Warp specialization: a warp's registers come from one SM sub-partition (16K registers), so a
+  // producer warp holding the consumers' register count wastes a consumer's share. In the
+  // warp-specialized layout warps 0-3 (one warpgroup; warp 0 produces, 1-3 exit) drop to
+  // REGS_PRODUCER registers and the consumer warpgroups rise to REGS_CONSUMER, which fills each
+  // sub-partition exactly: 40 + 2 x 232 (one CTA per SM) or 2 x (40 + 216) (two CTAs).
+  static constexpr int WS = (!PLAIN && SILU && W > 4 && W <= 8 && VEC == 8) ? CC1D_BWD_WS : 0;
+  static constexpr int WARPS = WS == 1 ? 8 : ((VEC == 8 || W > 8) ? 4 : 8);  // consumer warps = channel blocks per CTA
+  static constexpr int THREADS = WS ? 128 + WARPS * 32 : WARPS * 32 + 32;
+  static constexpr int PRODUCER_WARP = WS ? 0 : WARPS;
+  static constexpr int CONSUMER_WARP0 = WS ? 4 : 0;
+  static constexpr int REGS_PRODUCER = 40;
+  static constexpr int REGS_CONSUMER = WS == 1 ? 232 : 216;
+  // Registers per thread the launch must hold for the split (setmaxnreg.inc waits for them).
+  static constexpr int REGS_LAUNCH_MIN = WS ? (4 * REGS_PRODUCER + WARPS * REGS_CONSUMER + THREADS / 32 - 1) / (THREADS / 32) : 0;
   static constexpr int DG = WARPS * D_TILE;      // channels per CTA
   static constexpr int RS = 16;                  // rows per stage
   static constexpr int PAD = W - 1;
@@ -64,10 +89,12 @@ struct BwdCfg {
   static constexpr int SEQ_BYTES = (SROWS * 4 + 127) / 128 * 128;
   static constexpr int STAGE_BYTES = XBYTES + YBYTES + SEQ_BYTES;
   static constexpr int STAGES = 2;
-  // CTAs per SM the registers are bounded for: three up to W = 4, two for wider windows.
-  static constexpr int MIN_CTAS = W <= 4 ? 3 : 2;
+  // CTAs per SM the registers are bounded for: three up to W = 4, two for wider windows (one or
+  // two in the warp-specialized layouts).
+  static constexpr int MIN_CTAS = WS == 1 ? 1 : (WS == 2 ? 2 : (W <= 4 ? 3 : 2));
   static constexpr int SMEM_BYTES = kSmemAlign + kBarBytes + STAGES * STAGE_BYTES;
   static_assert(RS >= PAD, "dinit rows come from the last stage of a segment");
+  static_assert(!WS || REGS_LAUNCH_MIN * (THREADS / 32) <= 65536 / 32 / MIN_CTAS, "register split exceeds the SM");
 };
 
 struct alignas(64) BwdWalkParams {
@@ -124,9 +151,9 @@ struct SegmentWalk {
 };
 
 template <typename T, int W, bool SEQ, bool SILU, bool PLAIN>
-__global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU>::MIN_CTAS)
+__global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, W, SILU, PLAIN>::MIN_CTAS)
     cc1d_bwd_walk_kernel(const __grid_constant__ BwdWalkParams p) {
-  using C = BwdCfg<T, W, SILU>;
+  using C = BwdCfg<T, W, SILU, PLAIN>;
   constexpr int PAD = C::PAD, RS = C::RS, CPT = C::CPT, NP = C::NP, S = C::STAGES;
   constexpr int DT = C::D_TILE;
   constexpr bool FAST = sizeof(T) == 2;
@@ -162,7 +189,16 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
   __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == C::WARPS) {
+  if constexpr (C::WS != 0) {
+    // Every warp of a warpgroup takes part in its register change.
+    if (warp < 4) {
+      setmaxnreg_dec<C::REGS_PRODUCER>();
+      if (warp != C::PRODUCER_WARP) return;
+    } else {
+      setmaxnreg_inc<C::REGS_CONSUMER>();
+    }
+  }
+  if (warp == C::PRODUCER_WARP) {
     // ---------------- producer warp ----------------
     if (lane == 0 && !PLAIN) {
       prefetch_tensormap(&p.tmap_x);
@@ -234,7 +270,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU>::THREADS, BwdCfg<T, W, SILU
   }
 
   // ---------------- consumer warps: warp = channel block ----------------
-  const int blk = warp;
+  const int blk = warp - C::CONSUMER_WARP0;
   const bool blk_valid = blk < nvb;
   const int d = (g * C::WARPS + blk) * DT + lane * CPT;
   const bool dvalid = d < p.D;

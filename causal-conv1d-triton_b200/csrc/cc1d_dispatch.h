@@ -14,6 +14,7 @@ struct KernelInfo {
   int d_tile = 0;            // channels per CTA tile (per CTA channel group for the TMA backward)
   int t_tile = 0;            // time rows per CTA tile (per pipeline stage for the TMA backward)
   int box_d = 0;             // channels per TMA box (TMA backward: per consumer warp)
+  int min_regs = 0;          // registers per thread the launch must hold (warp-specialized backward)
 };
 
 // TMA path, template widths 2..8, 12 and 16; fn is null for other widths.

@@ -15,9 +15,9 @@ KernelInfo fwd_tma_one() {
 }
 template <typename T, int W, bool SEQ, bool SILU, bool PLAIN>
 KernelInfo bwd_tma_one() {
-  using C = BwdCfg<T, W, SILU>;
+  using C = BwdCfg<T, W, SILU, PLAIN>;
   return {reinterpret_cast<const void*>(&cc1d_bwd_walk_kernel<T, W, SEQ, SILU, PLAIN>), C::SMEM_BYTES, C::THREADS, C::DG,
-          C::RS, C::D_TILE};
+          C::RS, C::D_TILE, C::REGS_LAUNCH_MIN};
 }
 template <typename T, int W, bool PLAIN>
 KernelInfo fwd_tma_p(bool seq, bool silu) {
