@@ -533,12 +533,12 @@ int bwd_impl(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
         cudaLaunchKernel(pl.k.fn, dim3(static_cast<unsigned>(pl.grid)), dim3(pl.k.threads), args, pl.k.smem, stream));
   }
 
-  // Second stage: fixed-order sum over the P partial rows (32 column groups x 32 row slices per block).
+  // Second stage: fixed-order sum over the P partial rows (one warp per column group).
   const int64_t N = (W + 1) * D;
   const bool vec4 = N % 4 == 0 && reinterpret_cast<uintptr_t>(partials) % 16 == 0;
   const int64_t groups = vec4 ? N / 4 : N;
-  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(cdiv(groups, kReduceCols), 65535)));
-  const int rthreads = kReduceCols * kReduceSlices;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(cdiv(groups, kReduceWarps), 65535)));
+  const int rthreads = kReduceWarps * 32;
   if (vec4)
     cc1d_reduce_partials_kernel<4><<<blocks, rthreads, 0, stream>>>(partials, pl.P, static_cast<int>(D),
                                                                     static_cast<int>(W), dweight, weight_dtype,

@@ -10,13 +10,14 @@
 namespace cc1d {
 
 // Second stage of the dweight/dbias reduction (causal_conv1d.py:344-374): column n = k * D + d of
-// the (P, W+1, D) partials is summed over P in a fixed order (slice k of 32 sums rows k, k + 32, ...
-// in increasing order, then the 32 slice sums are added in order), so the result does not depend
-// on scheduling. All of a thread's loads are independent, so the whole buffer is in flight at once. Writes dweight[d, k] (k < W) and dbias[d] (k == W) in their own dtypes, or, when
-// grad_f32 is given, the fp32 vector [dweight (D, W) row-major, dbias (D)] instead (its dbias
-// part zero when there is no bias).
-constexpr int kReduceCols = 32;    // column groups per block
-constexpr int kReduceSlices = 32;  // partial rows are split over 32 warps: p = slice, slice + 32, ...
+// the (P, W+1, D) partials is summed over P in a fixed order, so the result does not depend on
+// scheduling. One warp per group of VEC adjacent columns: lane l sums rows l, l + 32, l + 64, ...
+// in increasing order (its loads are independent, so all of them are in flight at once), then
+// the 32 lane sums are combined by a fixed butterfly of shuffles. Eight warps per block, so that
+// even the headline shape's 1280 column groups spread over every SM. Writes dweight[d, k] (k < W)
+// and dbias[d] (k == W) in their own dtypes, or, when grad_f32 is given, the fp32 vector
+// [dweight (D, W) row-major, dbias (D)] instead (its dbias part zero when there is no bias).
+constexpr int kReduceWarps = 8;  // column groups per block, one warp each
 
 __device__ __forceinline__ void reduce_store(int64_t n, float t, int D, int W, void* dweight, int w_dtype,
                                              void* dbias, int b_dtype, float* grad_f32, int has_bias) {
@@ -33,47 +34,39 @@ __device__ __forceinline__ void reduce_store(int64_t n, float t, int D, int W, v
   }
 }
 
-// VEC = 4: each thread sums 4 adjacent columns with 16-byte loads (requires N % 4 == 0 and a
-// 16-byte aligned buffer); VEC = 1: one column per thread.
+// VEC = 4: each warp sums 4 adjacent columns with 16-byte loads (requires N % 4 == 0 and a
+// 16-byte aligned buffer); VEC = 1: one column per warp.
 template <int VEC>
-__global__ void __launch_bounds__(kReduceCols * kReduceSlices)
+__global__ void __launch_bounds__(kReduceWarps * 32)
     cc1d_reduce_partials_kernel(const float* __restrict__ partials, int P, int D, int W, void* dweight, int w_dtype,
                                 void* dbias, int b_dtype, float* grad_f32, int has_bias) {
-  __shared__ float part_sums[kReduceSlices][kReduceCols][VEC];
   const int64_t N = static_cast<int64_t>(W + 1) * D;
   const int64_t NG = N / VEC;  // column groups
-  const int c = threadIdx.x % kReduceCols, sl = threadIdx.x / kReduceCols;
-  for (int64_t g0 = static_cast<int64_t>(blockIdx.x) * kReduceCols; g0 < NG;
-       g0 += static_cast<int64_t>(gridDim.x) * kReduceCols) {
-    const int64_t gi = g0 + c;
+  const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+  for (int64_t gi = static_cast<int64_t>(blockIdx.x) * kReduceWarps + wi; gi < NG;
+       gi += static_cast<int64_t>(gridDim.x) * kReduceWarps) {
     float s[VEC];
 #pragma unroll
     for (int v = 0; v < VEC; ++v) s[v] = 0.0f;
-    if (gi < NG) {
-      const float* col = partials + gi * VEC;
-#pragma unroll 8
-      for (int q = sl; q < P; q += kReduceSlices) {
-        if constexpr (VEC == 4) {
-          const float4 x = __ldg(reinterpret_cast<const float4*>(col + static_cast<int64_t>(q) * N));
-          s[0] += x.x, s[1] += x.y, s[2] += x.z, s[3] += x.w;
-        } else {
-          s[0] += __ldg(col + static_cast<int64_t>(q) * N);
-        }
+    const float* col = partials + gi * VEC;
+#pragma unroll 4
+    for (int q = lane; q < P; q += 32) {
+      if constexpr (VEC == 4) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(col + static_cast<int64_t>(q) * N));
+        s[0] += x.x, s[1] += x.y, s[2] += x.z, s[3] += x.w;
+      } else {
+        s[0] += __ldg(col + static_cast<int64_t>(q) * N);
       }
     }
 #pragma unroll
-    for (int v = 0; v < VEC; ++v) part_sums[sl][c][v] = s[v];
-    __syncthreads();
-    if (sl == 0 && gi < NG) {
+    for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) {
-        float t = 0.0f;
+      for (int v = 0; v < VEC; ++v) s[v] += __shfl_down_sync(0xffffffffu, s[v], off);
+    if (lane == 0) {
 #pragma unroll
-        for (int k = 0; k < kReduceSlices; ++k) t += part_sums[k][c][v];
-        reduce_store(gi * VEC + v, t, D, W, dweight, w_dtype, dbias, b_dtype, grad_f32, has_bias);
-      }
+      for (int v = 0; v < VEC; ++v)
+        reduce_store(gi * VEC + v, s[v], D, W, dweight, w_dtype, dbias, b_dtype, grad_f32, has_bias);
     }
-    __syncthreads();
   }
 }
 
