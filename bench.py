@@ -876,8 +876,10 @@ def cfg5_sharded(args, dev, world, rank, dist):
     stream = torch.cuda.current_stream(dev)
     last = {}
 
-    def step(i):
+    def step(i, ev_mid=None):
         last["out"] = _fwd(x, w, b, None, None, None, True)
+        if ev_mid is not None:
+            ev_mid.record(stream)
         k = i % 2
         if pending[k] is not None:
             pending[k].wait()
@@ -906,7 +908,7 @@ def cfg5_sharded(args, dev, world, rank, dist):
     for i in range(K):
         ev[i][0].record(stream)
         last["out"] = None  # the previous step's output is released before the next is made
-        step(warm + i)
+        step(warm + i, ev[i][1])
         ev[i][2].record(stream)
     join()
     e.record(stream)
@@ -916,7 +918,11 @@ def cfg5_sharded(args, dev, world, rank, dist):
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = t.item() / K
-    step_us = sum(a[0].elapsed_time(a[2]) for a in ev) / K * 1e3
+    ft = torch.tensor([sum(a[0].elapsed_time(a[1]) for a in ev) / K * 1e3,
+                       sum(a[1].elapsed_time(a[2]) for a in ev) / K * 1e3], device=dev)
+    if dist is not None:
+        dist.all_reduce(ft, op=dist.ReduceOp.MAX)
+    fwd_us, bwd_us = ft.tolist()
     ar_us = allreduce_us(dist, flat[0].clone(), stream) if world > 1 else 0.0
 
     # Single-GPU full-batch reference on rank 0.
@@ -948,7 +954,8 @@ def cfg5_sharded(args, dev, world, rank, dist):
     return {
         "workload": "BASELINE config 5: B=64 T=8192 D=8192 W=8 bf16 bias+silu fwd+bwd, strong-scaled "
                     "(64/N rows per GPU), NCCL all-reduce of fp32 dweight||dbias (295 KB)",
-        "rows_per_gpu": nb, "steps": K, "ms_per_step": ms, "step_us_rank_events": step_us,
+        "rows_per_gpu": nb, "steps": K, "ms_per_step": ms, "fwd_us": fwd_us,
+        "bwd_us": bwd_us, "bwd_note": "backward kernel + reduce; the all-reduce runs on NCCL's stream",
         "allreduce_us": ar_us, "agg_gbs": agg, "frac_of_measured_per_gpu": agg / (world * peak),
         "peak": f"{kind} hbm_gbs {peak}", **res,
     }
