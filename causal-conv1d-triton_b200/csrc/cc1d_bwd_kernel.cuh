@@ -86,7 +86,9 @@ struct BwdCfg {
   static constexpr int SROWS = RS + 2 * PAD;     // seq rows a_lo - PAD .. a_lo + RS + PAD - 1
   static constexpr int XBYTES = WARPS * XROWS * ROW_BYTES;
   static constexpr int YBYTES = WARPS * RS * ROW_BYTES;
-  static constexpr int SEQ_BYTES = (SROWS * 4 + 127) / 128 * 128;
+  // seq_idx window of a stage, then one int: non-zero when the whole window is one sequence
+  // (ids equal and >= 0), where every mask of the stage passes.
+  static constexpr int SEQ_BYTES = ((SROWS + 1) * 4 + 127) / 128 * 128;
   static constexpr int STAGE_BYTES = XBYTES + YBYTES + SEQ_BYTES;
   static constexpr int STAGES = 2;
   // CTAs per SM the registers are bounded for: three up to W = 4, two for wider windows (one or
@@ -210,7 +212,9 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
       for (int j = n_st - 1; j >= 0 && ok; --j, ++i) {
         const int a_lo = s_lo + RS * j;  // processed top stage first: j = n_st - 1 .. 0
         const int s = i % S;
-        if (i >= S && !mbar_wait(&empty[s], ((i / S) - 1) & 1, p.status)) {
+        // The lanes leave together on a timeout (the seq_idx vote below is warp-wide).
+        const bool got = i < S || mbar_wait(&empty[s], ((i / S) - 1) & 1, p.status);
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
@@ -257,7 +261,15 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
         if constexpr (SEQ) {
           int* sq = reinterpret_cast<int*>(st + C::XBYTES + C::YBYTES);
           const int32_t* srow = p.seq + static_cast<int64_t>(b) * T_;
-          for (int r = lane; r < C::SROWS; r += 32) sq[r] = seq_at(srow, a_lo - PAD + r, T_, p.init != nullptr);
+          const int first = seq_at(srow, a_lo - PAD, T_, p.init != nullptr);
+          bool one = first >= 0;
+          for (int r = lane; r < C::SROWS; r += 32) {
+            const int v = seq_at(srow, a_lo - PAD + r, T_, p.init != nullptr);
+            sq[r] = v;
+            one = one && v == first;
+          }
+          one = __all_sync(0xffffffffu, one);
+          if (lane == 0) sq[C::SROWS] = one ? 1 : 0;
         }
         mbar_arrive(&full[s]);
         if constexpr (PLAIN) cp_async_mbar_arrive_noinc(&full[s]);
@@ -347,8 +359,11 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
           }
         };
 
-        auto step = [&](int s_, auto general) {
+        // masked: apply the seq_idx masks (false for stages whose window is one sequence, where
+        // every mask passes; the results are the same bits).
+        auto step = [&](int s_, auto general, auto masked) {
           constexpr bool GEN = decltype(general)::value;
+          constexpr bool SQ = SEQ && decltype(masked)::value;
           const int t = a_hi - s_;
           const int qs = RS - 1 - s_ + PAD;  // seq row of t
           if (s_ == 0) {
@@ -362,14 +377,14 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
           const bool own = !GEN || t < s_hi;
           float2 dz[NP];
           load_vec<T, CPT>(yt + (RS - 1 - s_) * DT, dz);
-          const int seq_t = SEQ ? sq[qs] : 0;
+          const int seq_t = SQ ? sq[qs] : 0;
           if constexpr (SILU) {
             float2 z[NP];
 #pragma unroll
             for (int i2 = 0; i2 < NP; ++i2) z[i2] = fmul2(w[PAD][i2], xr[s_][i2]);
 #pragma unroll
             for (int k = 0; k < PAD; ++k) {
-              if (!SEQ || sq[qs - PAD + k] == seq_t) {
+              if (!SQ || sq[qs - PAD + k] == seq_t) {
 #pragma unroll
                 for (int i2 = 0; i2 < NP; ++i2) z[i2] = ffma2(w[k][i2], xr[s_ + PAD - k][i2], z[i2]);
               }
@@ -388,7 +403,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
               }
             }
           }
-          if ((SEQ && seq_t < 0) || above) {
+          if ((SQ && seq_t < 0) || above) {
 #pragma unroll
             for (int i2 = 0; i2 < NP; ++i2) dz[i2] = make_float2(0.f, 0.f);
           }
@@ -403,7 +418,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
           for (int i2 = 0; i2 < NP; ++i2) gx[i2] = fmul2(w[PAD][i2], dz[i2]);
 #pragma unroll
           for (int j = 1; j <= PAD; ++j) {
-            if (!SEQ || sq[qs + j] == seq_t) {
+            if (!SQ || sq[qs + j] == seq_t) {
 #pragma unroll
               for (int i2 = 0; i2 < NP; ++i2) gx[i2] = ffma2(w[PAD - j][i2], dzall[PAD + s_ - j][i2], gx[i2]);
             }
@@ -421,7 +436,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
           // dweight / dbias partial sums (causal_conv1d.py:313-321).
 #pragma unroll
           for (int k = 0; k < PAD; ++k) {
-            if (!SEQ || sq[qs - PAD + k] == seq_t) {
+            if (!SQ || sq[qs - PAD + k] == seq_t) {
 #pragma unroll
               for (int i2 = 0; i2 < NP; ++i2) dw[k][i2] = ffma2(dz[i2], xr[s_ + PAD - k][i2], dw[k][i2]);
             }
@@ -435,12 +450,15 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
 
         const bool interior = a_hi < s_hi && a_lo - PAD >= 0 && dvalid &&
                               !(p.dfinal != nullptr && a_hi >= T_ - PAD);
-        if (interior) {
+        if (interior && SEQ && sq[C::SROWS] != 0) {
 #pragma unroll
-          for (int s_ = 0; s_ < RS; ++s_) step(s_, std::false_type{});
+          for (int s_ = 0; s_ < RS; ++s_) step(s_, std::false_type{}, std::false_type{});
+        } else if (interior) {
+#pragma unroll
+          for (int s_ = 0; s_ < RS; ++s_) step(s_, std::false_type{}, std::true_type{});
         } else {
 #pragma unroll
-          for (int s_ = 0; s_ < RS; ++s_) step(s_, std::true_type{});
+          for (int s_ = 0; s_ < RS; ++s_) step(s_, std::true_type{}, std::true_type{});
         }
         // Carry the dz of this stage's lowest PAD rows into the next stage.
 #pragma unroll

@@ -266,9 +266,16 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   }
   // seq_idx window of the tile: rows t0 - PAD .. t0 + T_TILE - 1
   int* sq = reinterpret_cast<int*>(tile + L::XBYTES);
+  bool one_seq = false;  // the whole window is one sequence (ids equal and >= 0): every mask passes
   if constexpr (SEQ) {
     const int32_t* srow = p.seq + static_cast<int64_t>(b) * p.T;
-    for (int r = threadIdx.x; r < L::XROWS; r += C::CONSUMERS) sq[r] = seq_at(srow, t0 - PAD + r, p.T, p.init != nullptr);
+    const int first = seq_at(srow, t0 - PAD, p.T, p.init != nullptr);
+    one_seq = first >= 0;
+    for (int r = threadIdx.x; r < L::XROWS; r += C::CONSUMERS) {
+      const int v = seq_at(srow, t0 - PAD + r, p.T, p.init != nullptr);
+      sq[r] = v;
+      one_seq = one_seq && v == first;
+    }
   }
 
   const int d = db * DT + lane * CPT;
@@ -282,7 +289,11 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   }
   if constexpr (SILU && FAST) halve_taps<W, NP>(w, bv);  // z below is h = z / 2
   const int pw = p.W - 1, off = W - p.W;  // true state rows; leading zero taps
-  __syncthreads();  // barrier initialised (or tile filled), seq window written
+  // barrier initialised (or tile filled), seq window written; with seq_idx, the tile-wide vote
+  if constexpr (SEQ)
+    one_seq = __syncthreads_and(one_seq) != 0;
+  else
+    __syncthreads();
   if (!PLAIN && !mbar_wait(full, 0, p.status)) {
     // Gave up (status recorded). The tile copy may still be landing in this CTA's shared memory:
     // wait for it once more, again bounded, before the CTA exits.
@@ -315,25 +326,29 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
 
   T* orow = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.T + ts) * D + d;
   const bool full_rows = dvalid && ts + R <= p.T;
+  // masked: apply the seq_idx masks (false for a tile whose window is one sequence, where every
+  // mask passes; the results are the same bits).
+  auto rows = [&](auto masked) {
+  constexpr bool SQ = SEQ && decltype(masked)::value;
   static_for<0, R>([&](auto rc) {
     constexpr int r = decltype(rc)::value;
     constexpr int cur = (r + PAD) % NW;
     load_vec<T, CPT>(xt + (rb + PAD + r) * DT, xw[cur]);
-    const int seq_t = SEQ ? sq[rb + PAD + r] : 0;
+    const int seq_t = SQ ? sq[rb + PAD + r] : 0;
     // z = w[PAD] x[t], then taps k = 0..PAD-1 oldest first, then bias (causal_conv1d.py:129-136).
     float2 z[NP];
 #pragma unroll
     for (int i2 = 0; i2 < NP; ++i2) z[i2] = fmul2(w[PAD][i2], xw[cur][i2]);
 #pragma unroll
     for (int k = 0; k < PAD; ++k) {
-      if (!SEQ || sq[rb + r + k] == seq_t) {
+      if (!SQ || sq[rb + r + k] == seq_t) {
 #pragma unroll
         for (int i2 = 0; i2 < NP; ++i2) z[i2] = ffma2(w[k][i2], xw[(r + k) % NW][i2], z[i2]);
       }
     }
 #pragma unroll
     for (int i2 = 0; i2 < NP; ++i2) z[i2] = fadd2(z[i2], bv[i2]);
-    if (SEQ && seq_t < 0) {
+    if (SQ && seq_t < 0) {
 #pragma unroll
       for (int i2 = 0; i2 < NP; ++i2) z[i2] = make_float2(0.f, 0.f);
     }
@@ -343,6 +358,11 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
     }
     if (full_rows || (dvalid && ts + r < p.T)) store_vec<T, CPT>(orow + r * D, z);
   });
+  };
+  if (SEQ && one_seq)
+    rows(std::false_type{});
+  else
+    rows(std::true_type{});
 
   // final_states = last W-1 rows (true width) of concat(initial_states, x) (causal_conv1d.py:153-164).
   if (p.final_states != nullptr && tt == p.n_tt - 1 && rg == 0 && dvalid) {
