@@ -640,10 +640,15 @@ int cc1d_fwd(const void* x, int64_t stride_x_batch, int64_t stride_x_time, const
       p.n_tt = static_cast<int>(cdiv(T, k.t_tile));
       p.n_db = static_cast<int>(cdiv(D, k.d_tile));
       p.w_dtype = weight_dtype, p.b_dtype = bias_dtype, p.init_dtype = init_dtype;
-      const int64_t grid = B * p.n_tt * p.n_db;  // one CTA per (batch row, time tile, channel block)
+      // One CTA per (channel block, time tile, batch row): a 3-D grid when the time tiles and batch
+      // rows fit its y and z limits (no index arithmetic in the kernel), else a flat one.
+      const int64_t grid = B * p.n_tt * p.n_db;
       if (grid >= (int64_t(1) << 31)) return CC1D_ERR_INVALID;
+      const dim3 g3 = (p.n_tt <= 65535 && B <= 65535)
+                          ? dim3(static_cast<unsigned>(p.n_db), static_cast<unsigned>(p.n_tt), static_cast<unsigned>(B))
+                          : dim3(static_cast<unsigned>(grid));
       void* args[] = {&p};
-      CC1D_TRY_CUDA(cudaLaunchKernel(k.fn, dim3(static_cast<unsigned>(grid)), dim3(k.threads), args, k.smem, stream));
+      CC1D_TRY_CUDA(cudaLaunchKernel(k.fn, g3, dim3(k.threads), args, k.smem, stream));
       return CC1D_OK;
     }
   }

@@ -226,11 +226,15 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   unsigned char* tile = smem + kBarBytes;
 
-  // blockIdx.x -> (channel block fastest, then time tile, then batch row)
-  const int db = blockIdx.x % p.n_db;
-  const int rest = blockIdx.x / p.n_db;
-  const int tt = rest % p.n_tt;
-  const int b = rest / p.n_tt;
+  // (channel block fastest, then time tile, then batch row): the block's (x, y, z) index when the
+  // grid is 3-D, else its x index decomposed (grids beyond 65535 time tiles or batch rows).
+  int db = blockIdx.x, tt = blockIdx.y, b = blockIdx.z;
+  if (gridDim.y == 1 && gridDim.z == 1 && (p.n_tt > 1 || p.B > 1)) {
+    db = blockIdx.x % p.n_db;
+    const int rest = blockIdx.x / p.n_db;
+    tt = rest % p.n_tt;
+    b = rest / p.n_tt;
+  }
   const int t0 = tt * C::T_TILE;
   const int rg = threadIdx.x / C::LANES_D, lane = threadIdx.x % C::LANES_D;
 
@@ -324,7 +328,7 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
     for (int k = 0; k < PAD; ++k) load_vec<T, CPT>(xt + (rb + k) * DT, xw[k]);
   }
 
-  T* orow = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.T + ts) * D + d;
+  T* orow = static_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.T + ts) * D + d;  // advanced one row per step
   const bool full_rows = dvalid && ts + R <= p.T;
   // masked: apply the seq_idx masks (false for a tile whose window is one sequence, where every
   // mask passes; the results are the same bits).
@@ -356,7 +360,8 @@ __global__ void __launch_bounds__(TileCfg<T, W>::CONSUMERS, FwdLayout<T, W, SEQ>
 #pragma unroll
       for (int i2 = 0; i2 < NP; ++i2) z[i2] = FAST ? silu2_of_half(z[i2]) : silu2<false>(z[i2]);
     }
-    if (full_rows || (dvalid && ts + r < p.T)) store_vec<T, CPT>(orow + r * D, z);
+    if (full_rows || (dvalid && ts + r < p.T)) store_vec<T, CPT>(orow, z);
+    orow += D;
   });
   };
   if (SEQ && one_seq)

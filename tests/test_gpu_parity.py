@@ -220,6 +220,14 @@ def test_ragged_sizes(cc, B, T, D, W):
                     has_seq=False, ret_final=True, dfinal=True, need_dinit=True, seed=B * T + D)
 
 
+@pytest.mark.parametrize("seq", [False, True])
+def test_more_batch_rows_than_a_grid_dimension(cc, seq):
+    """More than 65535 batch rows: the forward's grid cannot be 3-D (channel block, time tile, batch
+    row) and falls back to a flat grid whose index the kernel decomposes."""
+    check_vs_oracle(cc, 70000, 3, 64, 4, torch.bfloat16, has_bias=True, silu=True, has_init=True,
+                    has_seq=seq, ret_final=not seq, dfinal=not seq, need_dinit=True, seed=70000)
+
+
 def test_bf16_weights(cc):
     check_vs_oracle(cc, 2, 90, 64, 4, torch.bfloat16, has_bias=True, silu=True, has_init=True,
                     has_seq=False, ret_final=True, dfinal=True, need_dinit=True, seed=5,
