@@ -359,12 +359,15 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
           }
         };
 
+        // dx row of step s_ (row a_hi - s_), moved down one row per step.
+        T* dxrow = static_cast<T*>(p.dx) + b * p.sdxb + static_cast<int64_t>(a_hi) * p.sdxt + d;
         // masked: apply the seq_idx masks (false for stages whose window is one sequence, where
         // every mask passes; the results are the same bits).
         auto step = [&](int s_, auto general, auto masked) {
           constexpr bool GEN = decltype(general)::value;
           constexpr bool SQ = SEQ && decltype(masked)::value;
           const int t = a_hi - s_;
+          if (s_ > 0) dxrow -= p.sdxt;
           const int qs = RS - 1 - s_ + PAD;  // seq row of t
           if (s_ == 0) {
 #pragma unroll
@@ -432,7 +435,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
               for (int i2 = 0; i2 < NP; ++i2) gx[i2] = fadd2(gx[i2], v[i2]);
             }
           }
-          if (!GEN || dvalid) store_vec<T, CPT>(static_cast<T*>(p.dx) + b * p.sdxb + t * p.sdxt + d, gx);
+          if (!GEN || dvalid) store_vec<T, CPT>(dxrow, gx);
           // dweight / dbias partial sums (causal_conv1d.py:313-321).
 #pragma unroll
           for (int k = 0; k < PAD; ++k) {
