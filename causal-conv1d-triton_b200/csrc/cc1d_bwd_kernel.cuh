@@ -50,7 +50,9 @@ constexpr int kMaxDoutPieces = 4;
 // producer warpgroup and one consumer warpgroup; 0: the 5-warp walk. The producer warpgroup gives
 // its registers to the consumers with setmaxnreg (see BwdCfg). Measured on B200 at B=16 T=8192
 // D=8192 W=8 bf16 with SiLU: 1530 / 1635 / 1866 us for 1 / 2 / 0 (without SiLU, where the walk is
-// bound by its data movement, layout 1 is 5 % slower and 2 equal to 0).
+// bound by its data movement, layout 1 is 5 % slower and 2 equal to 0). Four consumer warpgroups
+// of 2-channel lanes (104 registers each) measured 1758 us against 1479 us for layout 1: at W = 8
+// the per-row loads, conversions and loop work per channel count more than the extra warps.
 #ifndef CC1D_BWD_WS
 #define CC1D_BWD_WS 1
 #endif
@@ -384,7 +386,7 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
           if constexpr (SILU) {
             float2 z[NP];
 #pragma unroll
-            for (int i2 = 0; i2 < NP; ++i2) z[i2] = fmul2(w[PAD][i2], xr[s_][i2]);
+            for (int i2 = 0; i2 < NP; ++i2) z[i2] = ffma2(w[PAD][i2], xr[s_][i2], bv[i2]);
 #pragma unroll
             for (int k = 0; k < PAD; ++k) {
               if (!SQ || sq[qs - PAD + k] == seq_t) {
@@ -394,7 +396,6 @@ __global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, 
             }
 #pragma unroll
             for (int i2 = 0; i2 < NP; ++i2) {
-              z[i2] = fadd2(z[i2], bv[i2]);
               // dz = dy * sig * (1 + z * (1 - sig))   (causal_conv1d.py:285-286)
               if constexpr (HALF) {
                 dz[i2] = dsilu2_of_half(z[i2], dz[i2]);  // z holds h = z / 2; this is 2 dz

@@ -191,13 +191,13 @@ __device__ __forceinline__ float2 tanh2(float2 h) { return make_float2(tanh_appr
 
 __device__ __forceinline__ float2 silu2_of_half(float2 h) { return ffma2(h, tanh2(h), h); }
 
-// dy * 2 SiLU'(z) from h = z / 2.
+// dy * 2 SiLU'(z) from h = z / 2, in three multiply-adds: 1 + t + h (1 - t^2) factors as
+// (1 + t) (1 + h (1 - t)).
 __device__ __forceinline__ float2 dsilu2_of_half(float2 h, float2 dy) {
-  const float2 m1 = make_float2(-1.f, -1.f);
   const float2 t = tanh2(h);
-  const float2 c = ffma2(t, t, m1);  // t^2 - 1
-  const float2 m = ffma2(h, c, m1);  // h (t^2 - 1) - 1
-  return fmul2(dy, ffma2(m, m1, t));  // dy (1 + t + h (1 - t^2))
+  const float2 g = ffma2(dy, t, dy);                      // dy (1 + t)
+  const float2 e = ffma2(h, make_float2(-t.x, -t.y), h);  // h (1 - t)
+  return ffma2(g, e, g);
 }
 
 // ---------------------------------------------------------------------------------------------
