@@ -214,10 +214,10 @@ KernelInfo fwd_tma_for(int dtype, int W, bool seq, bool silu, bool plain) {
   if (dtype == kF16) return fwd_tma_info<__half>(W, seq, silu, plain);
   return fwd_tma_info<float>(W, seq, silu, plain);
 }
-KernelInfo bwd_tma_for(int dtype, int W, bool seq, bool silu, bool plain) {
-  if (dtype == kBF16) return bwd_tma_info<__nv_bfloat16>(W, seq, silu, plain);
-  if (dtype == kF16) return bwd_tma_info<__half>(W, seq, silu, plain);
-  return bwd_tma_info<float>(W, seq, silu, plain);
+KernelInfo bwd_tma_for(int dtype, int W, bool seq, bool silu, bool plain, bool long_stages = false) {
+  if (dtype == kBF16) return bwd_tma_info<__nv_bfloat16>(W, seq, silu, plain, long_stages);
+  if (dtype == kF16) return bwd_tma_info<__half>(W, seq, silu, plain, long_stages);
+  return bwd_tma_info<float>(W, seq, silu, plain, long_stages);
 }
 KernelInfo fwd_generic_for(int dtype, int W) {
   if (dtype == kBF16) return fwd_generic_info<__nv_bfloat16>(W);
@@ -261,6 +261,10 @@ struct BwdPlan {
   int64_t ws_bytes = 0;
 };
 
+// Rows per CTA from which the backward's warp-specialized walk uses 24-row stages (measured on B200:
+// 7282 rows per CTA 3 % faster, 2260 rows equal, 886 rows 7 % slower than with 16-row stages).
+constexpr int64_t kLongWalkRows = 2048;
+
 int plan_bwd_uncached(const void* x, int64_t sxb, int64_t sxt, const void* dy, int64_t syb, int64_t syt, int64_t B,
                       int64_t T, int64_t D, int64_t W, int x_dtype, bool seq, bool silu, const DeviceInfo& di, int dev,
                       BwdPlan* pl) {
@@ -279,9 +283,8 @@ int plan_bwd_uncached(const void* x, int64_t sxb, int64_t sxt, const void* dy, i
     // one CTA of 1024 channels per SM); the workspace query sees neither flag, so the workspace is
     // sized for the largest partial count of the four, and each launch uses its own.
     int64_t p_max = 1;
-    for (int v = 0; v < 4; ++v) {
-      const bool vseq = (v & 1) != 0, vsilu = (v & 2) != 0;
-      const KernelInfo kv = bwd_tma_for(x_dtype, pl->wt, vseq, vsilu, pl->plain);
+    // Stretch of rows per CTA and partial count for one kernel variant.
+    auto split = [&](const KernelInfo& kv, int64_t* rpp, int64_t* P) -> int {
       if (kv.fn == nullptr) return CC1D_ERR_INVALID;
       if (kv.min_regs > 0) {
         // A warp-specialized kernel moves registers between its warpgroups with setmaxnreg; the
@@ -296,8 +299,26 @@ int plan_bwd_uncached(const void* x, int64_t sxb, int64_t sxt, const void* dy, i
       const int64_t rs = kv.t_tile;
       const int64_t cap = static_cast<int64_t>(di.sms) * o;
       const int64_t pw = std::max<int64_t>(1, std::min<int64_t>(cdiv(rows, rs), cap / n_blk));
-      const int64_t rpp = cdiv(cdiv(rows, pw), rs) * rs;
-      const int64_t P = cdiv(rows, rpp);
+      *rpp = cdiv(cdiv(rows, pw), rs) * rs;
+      *P = cdiv(rows, *rpp);
+      return CC1D_OK;
+    };
+    for (int v = 0; v < 4; ++v) {
+      const bool vseq = (v & 1) != 0, vsilu = (v & 2) != 0;
+      KernelInfo kv = bwd_tma_for(x_dtype, pl->wt, vseq, vsilu, pl->plain);
+      int64_t rpp = 0, P = 0;
+      CC1D_TRY(split(kv, &rpp, &P));
+      // Walks of at least kLongWalkRows rows per CTA take the 24-row-stage kernel where there is
+      // one (the warp-specialized layout); shorter ones keep 16-row stages, whose ring fills and
+      // drains faster.
+      if (rpp >= kLongWalkRows) {
+        const KernelInfo kl = bwd_tma_for(x_dtype, pl->wt, vseq, vsilu, pl->plain, true);
+        if (kl.fn != kv.fn) {
+          kv = kl;
+          CC1D_TRY(split(kv, &rpp, &P));
+        }
+      }
+      const int64_t n_blk = cdiv(D, kv.d_tile);
       p_max = std::max(p_max, P);
       if (vseq == seq && vsilu == silu) {
         pl->k = kv;

@@ -8,21 +8,22 @@
 // consumer warp: 128 channels of bf16/fp16 with SiLU, 64 without, 64 of fp32) and one contiguous
 // stretch of L rows of the
 // flattened (batch, time) index, i.e. one or two contiguous time segments of batch rows. It walks
-// each segment backwards in time, 16 rows per pipeline stage, from W-1 rows past the segment's end
+// each segment backwards in time, RS rows per pipeline stage (16, or 24 in the warp-specialized
+// layout), from W-1 rows past the segment's end
 // (the halo whose dz the segment's last dx rows need) down to the segment's first row, and then,
 // for the segment that starts at t = 0 when initial states need a gradient, to t = -(W-1). Because
 // the walk is continuous, every row's dz is computed once; only the W-1 halo rows per segment are
 // computed twice. The dz of the W-1 most recent rows, and all partial sums, stay in registers.
 //
 // Each CTA runs one producer warp, which issues per stage one TMA load of x (rows a_lo-(W-1) ..
-// a_lo+15) and one of dout (rows a_lo .. a_lo+15) per channel block into a 2-stage mbarrier ring
+// a_lo+RS-1) and one of dout (rows a_lo .. a_lo+RS-1) per channel block into a 2-stage mbarrier ring
 // and writes the stage's seq_idx window, and the consumer warps. With SiLU at template widths
 // 5..8 the CTA is warp-specialized: warpgroup 0 (whose warp 0 is the producer) gives up its
 // registers with setmaxnreg and two consumer warpgroups (8 channel blocks) take them, 232 per
 // thread instead of 168, one CTA per SM. Stages are aligned to the bottom of each segment, so the
 // last stage of a segment starts exactly at its first row; only the segment's top stage can be
 // partial. Consumer lanes own CPT consecutive channels (a 4- or 8-byte vector) and compute in fp32 pairs
-// with the sm_100 f32x2 instructions. A stage whose 16 rows all belong to the segment (no halo, no
+// with the sm_100 f32x2 instructions. A stage whose rows all belong to the segment (no halo, no
 // initial-state rows, no final-state rows, channels in range) runs a copy of the step loop without
 // any per-row checks.
 //
@@ -57,7 +58,7 @@ constexpr int kMaxDoutPieces = 4;
 #define CC1D_BWD_WS 1
 #endif
 
-template <typename T, int W, bool SILU, bool PLAIN = false>
+template <typename T, int W, bool SILU, bool PLAIN = false, bool LONG = false>
 struct BwdCfg {
   static constexpr int ES = static_cast<int>(sizeof(T));
   // bytes per lane: 8 with SiLU, above W = 4 and for fp32; 4 without SiLU up to W = 4 and for
@@ -82,7 +83,14 @@ struct BwdCfg {
   // Registers per thread the launch must hold for the split (setmaxnreg.inc waits for them).
   static constexpr int REGS_LAUNCH_MIN = WS ? (4 * REGS_PRODUCER + WARPS * REGS_CONSUMER + THREADS / 32 - 1) / (THREADS / 32) : 0;
   static constexpr int DG = WARPS * D_TILE;      // channels per CTA
-  static constexpr int RS = 16;                  // rows per stage
+  // Rows per stage: 16, or with LONG in the one-CTA warp-specialized layout 24, whose 2-stage ring
+  // still fits in shared memory (226 KB at W = 8). Longer stages spread the per-stage work (barrier
+  // waits, the W-1 halo rows of x loaded and converted again, the carried dz) over more rows, but
+  // take longer to fill and drain the ring: the host picks LONG for long walks only (B200, SiLU,
+  // bf16: 1476 -> 1430 us at B=16 T=8192 D=8192 W=8, 7282 rows per CTA; 477 -> 475 us at B=4
+  // T=16384 D=4352 W=8, 2260 rows; 191 -> 204 us at B=8 T=8192 D=2048 W=7, 886 rows).
+  static constexpr bool LONG_STAGES = LONG && WS == 1;
+  static constexpr int RS = LONG_STAGES ? 24 : 16;
   static constexpr int PAD = W - 1;
   static constexpr int XROWS = RS + PAD;         // x rows a_lo - PAD .. a_lo + RS - 1
   static constexpr int SROWS = RS + 2 * PAD;     // seq rows a_lo - PAD .. a_lo + RS + PAD - 1
@@ -154,10 +162,10 @@ struct SegmentWalk {
   }
 };
 
-template <typename T, int W, bool SEQ, bool SILU, bool PLAIN>
-__global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN>::THREADS, BwdCfg<T, W, SILU, PLAIN>::MIN_CTAS)
+template <typename T, int W, bool SEQ, bool SILU, bool PLAIN, bool LONG = false>
+__global__ void __launch_bounds__(BwdCfg<T, W, SILU, PLAIN, LONG>::THREADS, BwdCfg<T, W, SILU, PLAIN, LONG>::MIN_CTAS)
     cc1d_bwd_walk_kernel(const __grid_constant__ BwdWalkParams p) {
-  using C = BwdCfg<T, W, SILU, PLAIN>;
+  using C = BwdCfg<T, W, SILU, PLAIN, LONG>;
   constexpr int PAD = C::PAD, RS = C::RS, CPT = C::CPT, NP = C::NP, S = C::STAGES;
   constexpr int DT = C::D_TILE;
   constexpr bool FAST = sizeof(T) == 2;

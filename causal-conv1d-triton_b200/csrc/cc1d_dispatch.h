@@ -20,7 +20,8 @@ struct KernelInfo {
 // TMA path, template widths 2..8, 12 and 16; fn is null for other widths.
 // `plain`: the variant that copies its tiles with plain loads / cp.async chunks instead of TMA.
 template <typename T> KernelInfo fwd_tma_info(int W, bool seq, bool silu, bool plain);
-template <typename T> KernelInfo bwd_tma_info(int W, bool seq, bool silu, bool plain);
+// `long_stages`: the 24-row-stage kernel where the layout has one (see BwdCfg::LONG_STAGES).
+template <typename T> KernelInfo bwd_tma_info(int W, bool seq, bool silu, bool plain, bool long_stages);
 // Generic path, any width up to kGenericMaxWidth.
 template <typename T> KernelInfo fwd_generic_info(int W);
 template <typename T> KernelInfo bwd_generic_info(int W);

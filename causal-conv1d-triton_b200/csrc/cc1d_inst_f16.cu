@@ -3,7 +3,7 @@
 
 namespace cc1d {
 template KernelInfo fwd_tma_info<__half>(int, bool, bool, bool);
-template KernelInfo bwd_tma_info<__half>(int, bool, bool, bool);
+template KernelInfo bwd_tma_info<__half>(int, bool, bool, bool, bool);
 template KernelInfo fwd_generic_info<__half>(int);
 template KernelInfo bwd_generic_info<__half>(int);
 }  // namespace cc1d

@@ -17,6 +17,10 @@ Tolerances (tests/_tol.py): bf16 |a - e| <= 1e-2 + 1e-2 |e|, fp32 1e-5 in both t
 dweight / dbias (sums over B*T rows) within tol * max(1, max |e|). Bit-exact: the final states
 after every chunk of the config-3 chain, and out / dx at every config-4 padding row (exact zeros).
 
+Two further cases (not BASELINE configurations) give the backward walks of more than 2048 rows
+per CTA, where it switches to 24-row stages, with states, seq_idx packing and partial channel
+groups.
+
 Config 5 (B=64, T=8192, D=8192, W=8: 4.3e9 elements per tensor) is the only one whose element
 offsets pass 2^31; it exercises the kernels' 64-bit indexing. It holds about 52 GB on the device
 at its peak.
@@ -71,6 +75,14 @@ CONFIGS = {
     # Not a BASELINE config: cfg2's shape in fp32, held to the fp32 tolerance.
     "cfg2_B8_T8192_D1024_bias_silu_fp32": dict(B=8, T=8192, D=1024, W=4, w_std=0.5,
                                                b_std=0.1 ** 0.5, silu=True, dtype=torch.float32),
+    # Not BASELINE configs: walks long enough (more than 2048 rows per CTA) for the backward's
+    # 24-row-stage kernel, at widths 8 (chained chunks: initial and final states) and 5 (packed
+    # seq_idx with padding and initial states), with a partial last channel group (D = 7936) and
+    # stages that cross batch rows and end partial (T not a multiple of 24).
+    "long_walk_W8_B2_T40000_D7936_chain2": dict(B=2, T=40000, D=7936, W=8, w_std=8 ** -0.5,
+                                                b_std=0.1 ** 0.5, silu=True, init=True, chunks=2),
+    "long_walk_W5_B2_T40000_D7936_varlen": dict(B=2, T=40000, D=7936, W=5, w_std=5 ** -0.5,
+                                                b_std=0.1 ** 0.5, silu=True, init=True, varlen=True),
 }
 
 
