@@ -13,6 +13,11 @@ runs: the summed gradient is added to the leaf weight / bias .grad by a callback
 backward pass, as DistributedDataParallel does. The latter needs leaf parameters and
 Tensor.backward / torch.autograd.backward (not torch.autograd.grad).
 
+With `deterministic_grad_reduce=True` the sum is formed in a fixed order instead: the ranks'
+vectors are all-gathered and every rank adds them in rank order, so the gradient has the same bits
+on every rank and from run to run at a given world size, whichever algorithm the collective library
+picks (world x the vector's bytes cross the links instead of about 2x).
+
 The reference implementation has no distributed code; this is the data-parallel layer above its
 `causal_conv1d_fn` (causal_conv1d_triton/causal_conv1d.py:579-639), with the same arguments.
 """
@@ -54,6 +59,28 @@ def allreduce_flat_grad_(flat: Tensor, group=None) -> Tensor:
     return flat
 
 
+def gather_sum_flat_grad_(flat: Tensor, group=None, async_op: bool = False):
+    """Sums the flat fp32 gradient vector over the ranks of `group` in rank order, in place:
+    all-gathers the ranks' vectors, then flat = v_0 + v_1 + ... + v_{n-1} on every rank. Returns a
+    function that completes the sum (after waiting for the gather when `async_op`); nothing may
+    write `flat` before it is called."""
+    world = _world(group)
+    if world == 1:
+        return lambda: flat
+    parts = [torch.empty_like(flat) for _ in range(world)]
+    work = dist.all_gather(parts, flat, group=group, async_op=async_op)
+
+    def finish():
+        if async_op:
+            work.wait()
+        flat.copy_(parts[0])
+        for p in parts[1:]:
+            flat.add_(p)
+        return flat
+
+    return finish
+
+
 def split_flat_grad(flat: Tensor, dim: int, width: int, weight_dtype, bias_dtype=None):
     """(dweight (dim, width), dbias (dim) or None) from the flat vector, in the parameters' dtypes."""
     dweight = flat[: dim * width].view(dim, width)
@@ -73,7 +100,7 @@ def _accumulate(param: Tensor, grad: Tensor) -> None:
 
 
 def reduce_weight_grads(flat: Tensor, weight: Tensor, bias: Tensor | None, group=None,
-                        deferred: bool = False):
+                        deferred: bool = False, deterministic: bool = False):
     """The cross-rank sum of one conv's flat fp32 weight/bias gradient.
 
     deferred=False: all-reduces in place now and returns (dweight, dbias) for autograd to
@@ -81,18 +108,27 @@ def reduce_weight_grads(flat: Tensor, weight: Tensor, bias: Tensor | None, group
     tensors, after the work already queued on the current stream) and returns (None, None); a
     callback queued on the running backward pass waits for it and adds the result to weight.grad
     / bias.grad (which must be leaves) once every other node of the pass has run. Must be called
-    from inside a backward pass in that case."""
+    from inside a backward pass in that case. deterministic=True sums in rank order
+    (gather_sum_flat_grad_) instead of all-reducing."""
     D, W = weight.shape
     bias_dtype = bias.dtype if bias is not None else None
     if not deferred:
-        allreduce_flat_grad_(flat, group)
+        if deterministic:
+            gather_sum_flat_grad_(flat, group)()
+        else:
+            allreduce_flat_grad_(flat, group)
         return split_flat_grad(flat, D, W, weight.dtype, bias_dtype)
-    work = (dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=True)
-            if _world(group) > 1 else None)
+    gather_fin, work = None, None
+    if deterministic:
+        gather_fin = gather_sum_flat_grad_(flat, group, async_op=True)
+    elif _world(group) > 1:
+        work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group, async_op=True)
     stream = torch.cuda.current_stream(flat.device) if flat.is_cuda else None
 
     def finish():
         with torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext():
+            if gather_fin is not None:
+                gather_fin()  # waits for the gather, then adds in rank order
             if work is not None:
                 work.wait()  # the current stream (or, on the CPU, the host) waits for the sum
             dweight, dbias = split_flat_grad(flat, D, W, weight.dtype, bias_dtype)
@@ -110,7 +146,8 @@ class _ShardedFn(torch.autograd.Function):
     reference's `_CausalConv1dFn` (causal_conv1d.py:544-576) otherwise."""
 
     @staticmethod
-    def forward(ctx, x, weight, bias, seq_idx, initial_states, return_final_states, silu, group, overlap):
+    def forward(ctx, x, weight, bias, seq_idx, initial_states, return_final_states, silu, group, overlap,
+                deterministic):
         from .causal_conv1d import _fwd
 
         final_states = None
@@ -119,7 +156,7 @@ class _ShardedFn(torch.autograd.Function):
                                        dtype=x.dtype)
         out = _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu)
         ctx.save_for_backward(x, weight, bias, seq_idx, initial_states)
-        ctx.silu, ctx.group, ctx.overlap = silu, group, overlap
+        ctx.silu, ctx.group, ctx.overlap, ctx.deterministic = silu, group, overlap, deterministic
         # The deferred reduce adds to these leaves' .grad after the backward pass.
         ctx.leaves = (weight, bias) if overlap else None
         ctx.return_final_states = return_final_states
@@ -141,10 +178,11 @@ class _ShardedFn(torch.autograd.Function):
                                need_dinit, ctx.silu, grad_f32=flat)
         if ctx.overlap:
             weight, bias = ctx.leaves
-        dweight, dbias = reduce_weight_grads(flat, weight, bias, ctx.group, deferred=ctx.overlap)
+        dweight, dbias = reduce_weight_grads(flat, weight, bias, ctx.group, deferred=ctx.overlap,
+                                             deterministic=ctx.deterministic)
         if bias is None:
             dbias = None
-        return dx, dweight, dbias, None, dinit, None, None, None, None
+        return dx, dweight, dbias, None, dinit, None, None, None, None, None
 
 
 def sharded_causal_conv1d_fn(
@@ -158,6 +196,7 @@ def sharded_causal_conv1d_fn(
     activation: str | None = None,
     group=None,
     overlap_grad_reduce: bool = False,
+    deterministic_grad_reduce: bool = False,
 ) -> Tensor | tuple[Tensor, Tensor]:
     """Data-parallel causal_conv1d_fn. The arguments are the reference's (causal_conv1d.py:579-588)
     for this rank's rows: `x`, `seq_idx`, `initial_states` and `final_states_out` hold this rank's
@@ -167,7 +206,10 @@ def sharded_causal_conv1d_fn(
 
     overlap_grad_reduce: run the gradient all-reduce asynchronously and add its result to the leaf
     weight / bias .grad at the end of the backward pass (see the module docstring); requires leaf
-    weight and bias."""
+    weight and bias.
+
+    deterministic_grad_reduce: sum the ranks' gradients in rank order (all-gather, then add) so
+    they have the same bits on every rank and in every run at a given world size."""
     from .causal_conv1d import _channels_contiguous, _check_inputs, _tma_layout
 
     if activation not in (None, "silu", "swish"):
@@ -192,7 +234,7 @@ def sharded_causal_conv1d_fn(
     if needs_grad:
         x = _tma_layout(x, weight.shape[1])
         result = _ShardedFn.apply(x, weight, bias, seq_idx, initial_states, return_final_states, silu,
-                                  group, overlap_grad_reduce)
+                                  group, overlap_grad_reduce, deterministic_grad_reduce)
     else:
         from .causal_conv1d import _fwd
 

@@ -123,9 +123,9 @@ def _oracle_fn_class():
 
     class OracleShardFn(torch.autograd.Function):
         @staticmethod
-        def forward(ctx, x, weight, bias, seq, init, deferred):
+        def forward(ctx, x, weight, bias, seq, init, deferred, deterministic=False):
             ctx.save_for_backward(x, weight, bias, seq, init)
-            ctx.deferred = deferred
+            ctx.deferred, ctx.deterministic = deferred, deterministic
             ctx.leaves = (weight, bias)
             return torch.from_numpy(oracle.fwd(x, weight, bias, init, seq, silu=True))
 
@@ -136,9 +136,13 @@ def _oracle_fn_class():
                                            need_dinit=init is not None, silu=True)
             flat = torch.from_numpy(np.concatenate([dw.reshape(-1), db]))
             w_leaf, b_leaf = ctx.leaves
-            gw, gb = reduce_weight_grads(flat, w_leaf, b_leaf, deferred=ctx.deferred)
+            if ctx.deterministic:
+                torch.save(flat.clone(), os.path.join(os.environ["CC1D_TEST_OUT"],
+                                                      f"flat{dist.get_rank()}_{int(ctx.deferred)}.pt"))
+            gw, gb = reduce_weight_grads(flat, w_leaf, b_leaf, deferred=ctx.deferred,
+                                         deterministic=ctx.deterministic)
             gi = torch.from_numpy(dinit) if dinit is not None else None
-            return torch.from_numpy(dx), gw, gb, None, gi, None
+            return torch.from_numpy(dx), gw, gb, None, gi, None, None
 
     return OracleShardFn
 
@@ -204,3 +208,51 @@ def test_gloo_deferred_reduce_equals_immediate_on_packed_shards(tmp_path):
         assert torch.equal(r[rank][False][0], r[rank][True][0])
     # Each rank's dinit is its own rows' (no exchange).
     np.testing.assert_allclose(torch.cat([r[0][True][2], r[1][True][2]]).numpy(), rdi, rtol=1e-5, atol=1e-5)
+
+
+def _deterministic_worker(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), CC1D_TEST_OUT=result_dir)
+    import datetime
+    import sys
+
+    sys.path[:0] = [p for p in os.environ["CC1D_TEST_PATHS"].split(os.pathsep)]
+    from causal_conv1d_b200.distributed import shard_rows
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    Fn = _oracle_fn_class()
+    x, w, b, init, seq, dy = _varlen_inputs()
+    sl = shard_rows(x.shape[0], rank, world)
+    res = {}
+    for deferred in (False, True):
+        wl, bl = w.clone().requires_grad_(True), b.clone().requires_grad_(True)
+        il = init[sl].clone().requires_grad_(True)
+        out = Fn.apply(x[sl], wl, bl, seq[sl], il, deferred, True)
+        (out * dy[sl]).sum().backward()
+        res[deferred] = (wl.grad.clone(), bl.grad.clone())
+    torch.save(res, os.path.join(result_dir, f"det{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_gloo_deterministic_reduce_sums_in_rank_order(tmp_path):
+    """deterministic=True: every rank's weight/bias gradient is exactly v_0 + v_1 + v_2 (the ranks'
+    own flat vectors added in rank order), the same bits on every rank, immediate and deferred,
+    and within tolerance of the oracle's full-batch gradient; 3 ranks, uneven shards."""
+    from oracle import oracle
+
+    world = 3
+    os.environ["CC1D_TEST_PATHS"] = _paths()
+    mp.spawn(_deterministic_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    x, w, b, init, seq, dy = _varlen_inputs()
+    _, rdw, rdb, _ = oracle.bwd(x, w, b, init, seq, dy, None, need_dinit=True, silu=True)
+    D, W = w.shape
+    for deferred in (False, True):
+        v = [torch.load(tmp_path / f"flat{r}_{int(deferred)}.pt") for r in range(world)]
+        want = v[0].clone()
+        for p in v[1:]:
+            want += p
+        for r in range(world):
+            gw, gb = torch.load(tmp_path / f"det{r}.pt")[deferred]
+            assert torch.equal(gw.reshape(-1), want[: D * W]) and torch.equal(gb, want[D * W:])
+        np.testing.assert_allclose(gw.numpy(), rdw, rtol=1e-5, atol=1e-5 * np.abs(rdw).max())
+        np.testing.assert_allclose(gb.numpy(), rdb, rtol=1e-5, atol=1e-5 * np.abs(rdb).max())

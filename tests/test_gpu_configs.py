@@ -76,13 +76,20 @@ CONFIGS = {
     "cfg2_B8_T8192_D1024_bias_silu_fp32": dict(B=8, T=8192, D=1024, W=4, w_std=0.5,
                                                b_std=0.1 ** 0.5, silu=True, dtype=torch.float32),
     # Not BASELINE configs: walks long enough (more than 2048 rows per CTA) for the backward's
-    # 24-row-stage kernel, at widths 8 (chained chunks: initial and final states) and 5 (packed
-    # seq_idx with padding and initial states), with a partial last channel group (D = 7936) and
-    # stages that cross batch rows and end partial (T not a multiple of 24).
+    # 24-row-stage kernel, at widths 8 and 7 (chained chunks: initial and final states) and 5 and 6
+    # (packed seq_idx with padding and initial states), in bf16, fp16 and fp32, with a partial last
+    # channel group (D = 7936) and stages that cross batch rows and end partial (T not a multiple
+    # of 24).
     "long_walk_W8_B2_T40000_D7936_chain2": dict(B=2, T=40000, D=7936, W=8, w_std=8 ** -0.5,
                                                 b_std=0.1 ** 0.5, silu=True, init=True, chunks=2),
     "long_walk_W5_B2_T40000_D7936_varlen": dict(B=2, T=40000, D=7936, W=5, w_std=5 ** -0.5,
                                                 b_std=0.1 ** 0.5, silu=True, init=True, varlen=True),
+    "long_walk_W6_B2_T40000_D7936_varlen_fp16": dict(B=2, T=40000, D=7936, W=6, w_std=6 ** -0.5,
+                                                     b_std=0.1 ** 0.5, silu=True, init=True, varlen=True,
+                                                     dtype=torch.float16),
+    "long_walk_W7_B2_T40000_D7936_chain2_fp32": dict(B=2, T=40000, D=7936, W=7, w_std=7 ** -0.5,
+                                                     b_std=0.1 ** 0.5, silu=True, init=True, chunks=2,
+                                                     dtype=torch.float32),
 }
 
 

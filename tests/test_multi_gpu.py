@@ -5,6 +5,7 @@ identical on both ranks, while out, dx, dinit and the final states of each shard
 single-GPU results for those rows bit for bit. Three cases: plain bias + SiLU; packed
 variable-length rows (seq_idx with padding, initial states) with the all-reduce deferred to the
 end of the backward pass; chunked streaming state (initial and final states, final_states_out).
+The first two again with the rank-order (deterministic) gradient sum, immediate and deferred.
 Skipped with fewer than two GPUs."""
 
 import datetime
@@ -74,6 +75,11 @@ def _run(fn, t, dev, sl, **kw):
     return r
 
 
+# (result name, input case, deferred all-reduce, rank-order sum)
+CASES = [("plain", "plain", False, False), ("varlen", "varlen", True, False), ("stream", "stream", False, False),
+         ("plain_det", "plain", False, True), ("varlen_det", "varlen", True, True)]
+
+
 def _worker(rank, world, port, out_dir):
     import sys
 
@@ -86,10 +92,11 @@ def _worker(rank, world, port, out_dir):
     from causal_conv1d_b200.distributed import shard_rows, sharded_causal_conv1d_fn
 
     res = {}
-    for case, overlap in (("plain", False), ("varlen", True), ("stream", False)):
+    for name, case, overlap, det in CASES:
         t = _inputs(case)
         sl = shard_rows(t["x"].shape[0], rank, world)
-        res[case] = _run(sharded_causal_conv1d_fn, t, dev, sl, overlap_grad_reduce=overlap)
+        res[name] = _run(sharded_causal_conv1d_fn, t, dev, sl, overlap_grad_reduce=overlap,
+                         deterministic_grad_reduce=det)
     torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
@@ -103,12 +110,16 @@ def test_two_gpu_batch_shards_match_single_gpu(tmp_path):
     mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
     r = [torch.load(tmp_path / f"r{i}.pt") for i in range(2)]
     dev = torch.device("cuda", 0)
-    for case in ("plain", "varlen", "stream"):
-        a, c = r[0][case], r[1][case]
-        assert torch.equal(a["dw"], c["dw"]) and torch.equal(a["db"], c["db"]), case
+    for name, case, _, _ in CASES:
+        a, c = r[0][name], r[1][name]
+        assert torch.equal(a["dw"], c["dw"]) and torch.equal(a["db"], c["db"]), name
         full = _run(causal_conv1d_fn, _inputs(case), dev, slice(None))
         for k in ("out", "dx", "dinit", "final"):
             if k in full:
-                assert torch.equal(torch.cat([a[k], c[k]]), full[k]), f"{case}: {k}"
-        assert_close_sum(a["dw"], full["dw"], "bf16", f"{case}: dweight")
-        assert_close_sum(a["db"], full["db"], "bf16", f"{case}: dbias")
+                assert torch.equal(torch.cat([a[k], c[k]]), full[k]), f"{name}: {k}"
+        assert_close_sum(a["dw"], full["dw"], "bf16", f"{name}: dweight")
+        assert_close_sum(a["db"], full["db"], "bf16", f"{name}: dbias")
+    # Two ranks: the rank-order sum v_0 + v_1 and NCCL's sum of the same two vectors are one
+    # floating-point addition, so both modes give the same bits.
+    for name in ("plain", "varlen"):
+        assert torch.equal(r[0][name]["dw"], r[0][name + "_det"]["dw"]), name
