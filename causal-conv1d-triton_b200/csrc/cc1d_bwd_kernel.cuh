@@ -32,7 +32,8 @@
 // fixed-order reduction over P follows (cc1d_reduce_kernels.cuh).
 //
 // Reference: jxiong21029/causal-conv1d-triton, causal_conv1d_triton/causal_conv1d.py,
-// `_bwd_kernel` :167-341 (per-element arithmetic and its order, seq_idx conventions, dinit rows).
+// `_bwd_kernel` :167-341 (per-element arithmetic and its order, except that the recomputed z takes
+// the bias with its first tap; seq_idx conventions, dinit rows).
 #pragma once
 
 #include "cc1d_tma_kernels.cuh"
