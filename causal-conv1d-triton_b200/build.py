@@ -1,7 +1,8 @@
 """Builds libcausal_conv1d_b200.so (the C-ABI library of include/causal_conv1d_b200.h) for
 sm_100a with nvcc, in-tree: objects under _build/, the library inside the Python package; then the
-package's CPython binding of the hot entry points (csrc/cc1d_pyfast.c -> _cc1d_fast*.so), linked
-against that library.
+package's CPython binding of the hot entry points (csrc/cc1d_pyfast.c -> _cc1d_fast*.so) and its
+torch-side forward/backward launchers (csrc/cc1d_torch_ext.cpp -> _cc1d_torch*.so, host C++ against
+torch's headers), both linked against that library.
 
     python causal-conv1d-triton_b200/build.py [--force] [--verbose]
 """
@@ -24,6 +25,8 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "causal_conv1d_b200", "libcausal_conv1d_b200.so")
 FAST_SRC = os.path.join(CSRC, "cc1d_pyfast.c")
 FAST = os.path.join(HERE, "causal_conv1d_b200", "_cc1d_fast" + sysconfig.get_config_var("EXT_SUFFIX"))
+TORCH_SRC = os.path.join(CSRC, "cc1d_torch_ext.cpp")
+TORCH_EXT = os.path.join(HERE, "causal_conv1d_b200", "_cc1d_torch" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
@@ -93,6 +96,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     if lib_path == LIB:
         build_fast(force, verbose)
+        build_torch_ext(force, verbose)
     return lib_path
 
 
@@ -111,6 +115,34 @@ def build_fast(force: bool = False, verbose: bool = False) -> str:
     if r.returncode != 0:
         raise RuntimeError(f"binding build failed:\n{r.stdout}\n{r.stderr}")
     return FAST
+
+
+def build_torch_ext(force: bool = False, verbose: bool = False) -> str:
+    """Compiles the torch-side launchers (host C++, torch's headers and libraries) against the built
+    library."""
+    header = os.path.join(INCLUDE, "causal_conv1d_b200.h")
+    if not (force or _stale(TORCH_EXT, [TORCH_SRC, header, LIB])):
+        return TORCH_EXT
+    import torch
+    import torch.utils.cpp_extension as ce
+
+    cxx = shutil.which("g++") or "c++"
+    torch_lib = ce.library_paths()[0]
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(_nvcc())), "include")
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch.compiled_with_cxx11_abi())}",
+           "-DTORCH_EXTENSION_NAME=_cc1d_torch", "-DTORCH_API_INCLUDE_EXTENSION_H"]
+    for inc in ce.include_paths() + [cuda_inc, sysconfig.get_paths()["include"], INCLUDE]:
+        cmd += ["-I", inc]
+    cmd += [TORCH_SRC, "-L", os.path.dirname(LIB), "-lcausal_conv1d_b200", "-L", torch_lib, "-lc10", "-lc10_cuda",
+            "-ltorch", "-ltorch_cpu", "-ltorch_python", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}",
+            "-o", TORCH_EXT]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch launcher build failed:\n{r.stdout}\n{r.stderr}")
+    return TORCH_EXT
 
 
 if __name__ == "__main__":

@@ -2,9 +2,12 @@
 
 `lib` binds every entry point with ctypes. `fast` is the package's CPython binding of the hot
 launch entry points (cc1d_fwd, cc1d_bwd_workspace_bytes, cc1d_bwd, cc1d_update; built from
-csrc/cc1d_pyfast.c), which parses arguments in a fraction of ctypes' per-call time; both reach
-the same loaded library. Both are built in-tree by causal-conv1d-triton_b200/build.py. Importing
-this module without them raises ImportError: there is no CPU or Python fallback for the kernels.
+csrc/cc1d_pyfast.c), which parses arguments in a fraction of ctypes' per-call time. `tex` holds
+the forward and backward launchers written in C++ against torch (csrc/cc1d_torch_ext.cpp): they
+allocate the outputs and the workspace with torch's allocator and call cc1d_fwd / cc1d_bwd, which
+keeps the per-call host time of the autograd path low. All three reach the same loaded library and
+are built in-tree by causal-conv1d-triton_b200/build.py. Importing this module without them raises
+ImportError: there is no CPU or Python fallback for the kernels.
 """
 
 from __future__ import annotations
@@ -83,6 +86,15 @@ try:
     from . import _cc1d_fast as fast  # noqa: E402  (links libcausal_conv1d_b200.so, loaded above)
 except ImportError as e:  # pragma: no cover - only without a build
     raise ImportError(f"the package's CPython binding is missing ({e}): build the CUDA library first "
+                      "(python causal-conv1d-triton_b200/build.py)") from e
+
+
+try:
+    import torch  # noqa: E402,F401  (the launchers below link torch's libraries)
+
+    from . import _cc1d_torch as tex  # noqa: E402  (torch-side forward/backward launchers)
+except ImportError as e:  # pragma: no cover - only without a build
+    raise ImportError(f"the package's torch launchers are missing ({e}): build the CUDA library first "
                       "(python causal-conv1d-triton_b200/build.py)") from e
 
 

@@ -9,8 +9,9 @@ states are (batch, width - 1, dim): the inputs preceding x[:, 0]. Any width >= 2
 fp32/fp16/bf16 inputs, fp32 accumulation.
 
 The kernels are hand-written CUDA for sm_100a behind the C ABI of include/causal_conv1d_b200.h,
-called through ctypes (`_native`). This module keeps the host-side logic of the reference: the
-argument checks, the autograd Function, and the empty-input cases.
+called through the package's bindings (`_native`: ctypes, a CPython binding of the hot entry
+points, and torch-side forward/backward launchers in C++). This module keeps the host-side logic of
+the reference: the argument checks, the autograd Function, and the empty-input cases.
 """
 
 from __future__ import annotations
@@ -19,7 +20,7 @@ import torch
 from torch import Tensor
 
 from . import _native
-from ._native import DTYPE_CODE, check, fast, lib
+from ._native import DTYPE_CODE, check, fast, lib, tex
 
 _FLOAT = (torch.float32, torch.float16, torch.bfloat16)
 
@@ -111,103 +112,32 @@ class _DeviceGuard:
 
 
 def _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu):
-    """Host launcher of the forward (the reference's `_fwd`, causal_conv1d.py:433-472)."""
+    """Host launcher of the forward (the reference's `_fwd`, causal_conv1d.py:433-472): the output
+    allocation, device guard and stream come from the torch-side launcher (csrc/cc1d_torch_ext.cpp),
+    which calls cc1d_fwd."""
     if x.dtype not in _FLOAT:
         raise TypeError(f"x must be float32, float16 or bfloat16, got {x.dtype}")
-    B, T, D = x.shape
-    W = weight.shape[1]
-    dev = x.device
-    out = torch.empty(B, T, D, device=dev, dtype=x.dtype)
-    w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
-    with _DeviceGuard(dev):
-        rc = fast.fwd(
-            x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
-            _ptr(seq_idx), out.data_ptr(), _ptr(final_states), B, T, D, W,
-            DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
-            _stream(dev),
-        )
+    rc, out = tex.fwd(x, weight, bias, seq_idx, initial_states, final_states, bool(silu))
     if rc:
         check(rc, "causal_conv1d forward")
     return out
 
 
-# Workspace bytes of the backward by (device, dtype, sizes, strides, 16-byte alignment of x and
-# dout): the library's plan is a pure function of these, so a step need not re-plan through the
-# library to size its workspace.
-_WS_CACHE: dict = {}
-
-
-def _workspace_bytes(x, dout, B, T, D, W, dev_index):
-    key = (dev_index, x.dtype, B, T, D, W, x.stride(0), x.stride(1), dout.stride(0), dout.stride(1),
-           x.data_ptr() % 16, dout.data_ptr() % 16)
-    n = _WS_CACHE.get(key)
-    if n is None:
-        n = fast.bwd_workspace_bytes(x.data_ptr(), x.stride(0), x.stride(1), dout.data_ptr(),
-                                     dout.stride(0), dout.stride(1), B, T, D, W, DTYPE_CODE[x.dtype])
-        if n < 0:
-            check(_native.CC1D_ERR_INVALID, "causal_conv1d backward workspace")
-        if len(_WS_CACHE) > 4096:
-            _WS_CACHE.clear()
-        _WS_CACHE[key] = n
-    return n
-
-
 def _bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_dinit, silu,
          grad_f32=None, fuse_param_grads=True):
-    """Host launcher of the backward (the reference's `_bwd`, causal_conv1d.py:475-541).
+    """Host launcher of the backward (the reference's `_bwd`, causal_conv1d.py:475-541), through the
+    torch-side launcher (csrc/cc1d_torch_ext.cpp): it allocates dx, dinit, the gradients and the
+    workspace (cc1d_bwd_workspace_bytes) with torch's allocator and calls cc1d_bwd.
 
     Returns (dx, dweight, dbias, dinit). With `grad_f32` (a contiguous fp32 tensor of D * (W + 1)
     elements) the weight/bias gradients are written there as [dweight (D, W), dbias (D)] instead,
     and dweight/dbias are returned as None. With fp32 weight and bias and `fuse_param_grads`,
     dweight and dbias are views of one fp32 buffer (one allocation fewer per call).
     """
-    B, T, D = x.shape
-    W = weight.shape[1]
-    dev = x.device
-    dx = torch.empty(B, T, D, device=dev, dtype=x.dtype)
-    dinit = torch.empty_like(initial_states) if need_dinit else None
-    w, b, init = _as_float(weight), _as_float(bias), _as_float(initial_states)
-    dinit_k = _as_float(dinit)
-    flat = None
-    if grad_f32 is None:
-        if fuse_param_grads and weight.dtype == torch.float32 and (bias is None or bias.dtype == torch.float32):
-            # fp32 parameters: one allocation holds [dweight (D, W), dbias (D)], written by the
-            # kernel's fp32 gradient output; the gradients are views of it.
-            flat = torch.empty(D * (W + 1), device=dev, dtype=torch.float32)
-            dweight, dbias = None, None
-        else:
-            dweight = torch.empty_like(w)
-            dbias = torch.empty_like(b) if b is not None else None
-    else:
-        dweight = dbias = None
-    if dfinal_states is not None and dfinal_states.dtype != x.dtype:
-        dfinal_states = dfinal_states.to(x.dtype)
-    with _DeviceGuard(dev):
-        ws_bytes = _workspace_bytes(x, dout, B, T, D, W, dev.index)
-        workspace = torch.empty(max(1, ws_bytes // 4), device=dev, dtype=torch.float32)
-        rc = fast.bwd(
-            x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), _ptr(b), _ptr(init),
-            _ptr(seq_idx), dout.data_ptr(), dout.stride(0), dout.stride(1),
-            _ptr(dfinal_states), dx.data_ptr(), _ptr(dweight), _ptr(dbias), _ptr(dinit_k),
-            _ptr(grad_f32 if grad_f32 is not None else flat), workspace.data_ptr(), ws_bytes, B, T, D, W,
-            DTYPE_CODE[x.dtype], DTYPE_CODE[w.dtype], _code(b), _code(init), int(silu),
-            _stream(dev),
-        )
+    rc, dx, dweight, dbias, dinit = tex.bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states,
+                                            bool(need_dinit), bool(silu), grad_f32, bool(fuse_param_grads))
     if rc:
         check(rc, "causal_conv1d backward")
-    if dinit is not None and dinit_k is not dinit:
-        dinit.copy_(dinit_k)
-    if flat is not None:
-        if bias is not None:
-            dweight, dbias = flat.split((D * W, D))
-            dweight = dweight.view(D, W)
-        else:
-            dweight = flat[: D * W].view(D, W)
-    elif grad_f32 is None:
-        if dweight.dtype != weight.dtype:
-            dweight = dweight.to(weight.dtype)
-        if dbias is not None and dbias.dtype != bias.dtype:
-            dbias = dbias.to(bias.dtype)
     return dx, dweight, dbias, dinit
 
 

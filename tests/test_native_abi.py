@@ -183,3 +183,16 @@ def test_fast_binding_checks_arguments_and_returns_abi_codes():
         fast.bwd(*bwd, 0)
     with pytest.raises(TypeError):
         fast.fwd(*(["x"] + fwd[1:]))
+
+
+def test_torch_launchers_load_and_expose_forward_and_backward():
+    """The torch-side launchers (csrc/cc1d_torch_ext.cpp) load on the CPU, linked against the same
+    library, with the forward and backward entry points the autograd path calls."""
+    from causal_conv1d_b200 import _native
+
+    tex = _native.tex
+    assert callable(tex.fwd) and callable(tex.bwd)
+    assert "fwd(" in tex.fwd.__doc__ and "bwd(" in tex.bwd.__doc__
+    import os
+
+    assert os.path.dirname(tex.__file__) == os.path.dirname(_native.LIB_PATH)
