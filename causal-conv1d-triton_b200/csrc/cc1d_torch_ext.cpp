@@ -69,6 +69,7 @@ std::tuple<int, at::Tensor, c10::optional<at::Tensor>, c10::optional<at::Tensor>
   const int64_t B = x.size(0), T = x.size(1), D = x.size(2), W = weight.size(1);
   const c10::cuda::CUDAGuard guard(x.device());
   at::Tensor dx = at::empty({B, T, D}, x.options());
+  if (need_dinit && !initial_states.has_value()) return {CC1D_ERR_INVALID, dx, c10::nullopt, c10::nullopt, c10::nullopt};
   c10::optional<at::Tensor> dinit;
   if (need_dinit) dinit = at::empty_like(*initial_states);
   const at::Tensor w = as_float(weight);
