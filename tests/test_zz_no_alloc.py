@@ -29,9 +29,8 @@ def _p(t):
     return None if t is None else t.data_ptr()
 
 
-def _inputs(seed):
+def _inputs(seed, B=3, T=1000, D=384, W=4):
     g = torch.Generator().manual_seed(seed)
-    B, T, D, W = 3, 1000, 384, 4
     x = torch.randn(B, T, D, generator=g).to(torch.bfloat16).to(DEV)
     w = (torch.randn(D, W, generator=g) * 0.5).to(DEV)
     b = (torch.randn(D, generator=g) * 0.3).to(DEV)
@@ -45,13 +44,19 @@ def _outputs(x, w, b, init):
     return (torch.empty_like(x), torch.empty_like(w), torch.empty_like(b), torch.empty_like(init))
 
 
-def test_noalloc_matches_workspace_backward_twice():
+# A short walk (W = 4, 16-row stages) and one long enough for the warp-specialized W = 8 backward's
+# 24-row stages (18 CTAs per channel group, each walking about 4460 rows; 5.1 MB of partials).
+SHAPES = [(3, 1000, 384, 4), (2, 40000, 7936, 8)]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["W4_short", "W8_long_walk"])
+def test_noalloc_matches_workspace_backward_twice(shape):
     from causal_conv1d_b200 import _native
 
     lib = _native.lib
     stream = torch.cuda.current_stream().cuda_stream
     for seed in (1, 2):  # two calls in a row reuse the library's scratch array
-        x, w, b, init, dy, dfin = _inputs(seed)
+        x, w, b, init, dy, dfin = _inputs(seed, *shape)
         B, T, D = x.shape
         W = w.shape[1]
         args_in = (x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), b.data_ptr(),
