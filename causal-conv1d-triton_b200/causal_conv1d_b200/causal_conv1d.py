@@ -11,7 +11,8 @@ fp32/fp16/bf16 inputs, fp32 accumulation.
 The kernels are hand-written CUDA for sm_100a behind the C ABI of include/causal_conv1d_b200.h,
 called through the package's bindings (`_native`: ctypes, a CPython binding of the hot entry
 points, and torch-side forward/backward launchers in C++). This module keeps the host-side logic of
-the reference: the argument checks, the autograd Function, and the empty-input cases.
+the reference: the argument checks and the empty-input cases. Its autograd Function is C++
+(`ConvFn` in csrc/cc1d_torch_ext.cpp), which spares each call the Python Function machinery.
 """
 
 from __future__ import annotations
@@ -207,36 +208,6 @@ def _bwd_split(x, weight, bias, seq_idx, initial_states, dout_pieces, need_dinit
     return dweight, dbias, dinit
 
 
-class _CausalConv1dFn(torch.autograd.Function):
-    """Autograd wrapper (the reference's `_CausalConv1dFn`, causal_conv1d.py:544-576)."""
-
-    @staticmethod
-    def forward(ctx, x, weight, bias, seq_idx, initial_states, return_final_states, silu):
-        final_states = None
-        if return_final_states:
-            final_states = torch.empty(
-                x.shape[0], weight.shape[1] - 1, x.shape[2], device=x.device, dtype=x.dtype
-            )
-        out = _fwd(x, weight, bias, seq_idx, initial_states, final_states, silu)
-        ctx.save_for_backward(x, weight, bias, seq_idx, initial_states)
-        ctx.silu = silu
-        ctx.return_final_states = return_final_states
-        return (out, final_states) if return_final_states else out
-
-    @staticmethod
-    def backward(ctx, dout, *args):
-        x, weight, bias, seq_idx, initial_states = ctx.saved_tensors
-        dfinal_states = args[0] if ctx.return_final_states else None
-        if dfinal_states is not None:
-            dfinal_states = dfinal_states.contiguous()
-        need_dinit = initial_states is not None and ctx.needs_input_grad[4]
-        dout = _tma_layout(_channels_contiguous(dout), weight.shape[1])
-        dx, dweight, dbias, dinit = _bwd(
-            x, weight, bias, seq_idx, initial_states, dout, dfinal_states, need_dinit, ctx.silu,
-        )
-        return dx, dweight, dbias, None, dinit, None, None
-
-
 def causal_conv1d_fn(
     x: Tensor,
     weight: Tensor,
@@ -285,9 +256,11 @@ def causal_conv1d_fn(
         # The forward reads any layout; the backward's kernels need 16-byte aligned x, so a
         # misaligned x is copied once here and the copy is what the backward keeps.
         x = _tma_layout(x, weight.shape[1])
-        result = _CausalConv1dFn.apply(
-            x, weight, bias, seq_idx, initial_states, return_final_states, silu
-        )
+        # The reference's `_CausalConv1dFn` (causal_conv1d.py:544-576) as a C++ autograd Function
+        # (`ConvFn`, csrc/cc1d_torch_ext.cpp): same saved tensors, need_dinit rule and gradients. A
+        # failing library call inside it raises RuntimeError with the library's message.
+        res = tex.conv_fn(x, weight, bias, seq_idx, initial_states, return_final_states, silu)
+        result = (res[0], res[1]) if return_final_states else res[0]
     else:
         final_states = None
         if return_final_states:

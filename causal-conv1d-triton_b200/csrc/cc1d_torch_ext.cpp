@@ -109,11 +109,87 @@ std::tuple<int, at::Tensor, c10::optional<at::Tensor>, c10::optional<at::Tensor>
   return {rc, dx, dweight, dbias, dinit};
 }
 
+// Throws the library's error for a non-zero result code (inside the autograd Function, where the
+// code cannot be handed back to Python).
+void check_rc(int rc, const char* what) {
+  TORCH_CHECK(rc == CC1D_OK, what, ": ", cc1d_error_string(rc), rc == CC1D_ERR_CUDA ? " (cudaError " : "",
+              rc == CC1D_ERR_CUDA ? std::to_string(cc1d_last_cuda_error()) + ")" : std::string());
+}
+
+// `t` itself, or a contiguous copy when its channel stride is not 1 or when its rows could feed the
+// TMA kernels (width <= 16, channels x element size a multiple of 16 bytes) but its base or
+// batch/time strides are not 16-byte multiples (the rule of the package's _tma_layout).
+at::Tensor tma_layout(const at::Tensor& t0, int64_t width) {
+  const at::Tensor t = t0.stride(-1) == 1 ? t0 : t0.contiguous();
+  const int64_t B = t.size(0), D = t.size(2), es = t.element_size();
+  if (width > 16 || (D * es) % 16 != 0 || t.numel() == 0) return t;
+  const bool aligned = reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0 && (t.stride(1) * es) % 16 == 0 &&
+                       (B == 1 || (t.stride(0) * es) % 16 == 0);
+  return aligned ? t : t.clone(at::MemoryFormat::Contiguous);
+}
+
+// The reference's `_CausalConv1dFn` (causal_conv1d.py:544-576) as a C++ autograd Function: the same
+// saved tensors, the same need_dinit rule and the same gradients, without the Python-level
+// Function machinery on every call. Absent tensors come in as empty optionals, which the autograd
+// machinery treats as non-tensor arguments (no edge), so needs_input_grad counts only the tensors
+// given.
+struct ConvFn : public torch::autograd::Function<ConvFn> {
+  static torch::autograd::variable_list forward(torch::autograd::AutogradContext* ctx, const at::Tensor& x,
+                                                const at::Tensor& weight, const c10::optional<at::Tensor>& bias,
+                                                const c10::optional<at::Tensor>& seq_idx,
+                                                const c10::optional<at::Tensor>& initial_states,
+                                                bool return_final_states, bool silu) {
+    c10::optional<at::Tensor> final_states;
+    if (return_final_states) final_states = at::empty({x.size(0), weight.size(1) - 1, x.size(2)}, x.options());
+    auto [rc, out] = fwd(x, weight, bias, seq_idx, initial_states, final_states, silu);
+    check_rc(rc, "causal_conv1d forward");
+    ctx->save_for_backward({x, weight, bias.value_or(at::Tensor()), seq_idx.value_or(at::Tensor()),
+                            initial_states.value_or(at::Tensor())});
+    ctx->saved_data["silu"] = silu;
+    ctx->saved_data["final"] = return_final_states;
+    // Edge index of initial_states among the tensor inputs given (x, weight, [bias], [seq_idx]).
+    ctx->saved_data["init_edge"] =
+        static_cast<int64_t>(2 + (bias.has_value() ? 1 : 0) + (seq_idx.has_value() ? 1 : 0));
+    if (return_final_states) return {out, *final_states};
+    return {out};
+  }
+
+  static torch::autograd::variable_list backward(torch::autograd::AutogradContext* ctx,
+                                                 torch::autograd::variable_list grads) {
+    const auto saved = ctx->get_saved_variables();
+    const at::Tensor &x = saved[0], &weight = saved[1], &bias = saved[2], &seq_idx = saved[3], &init = saved[4];
+    auto opt = [](const at::Tensor& t) { return t.defined() ? c10::optional<at::Tensor>(t) : c10::nullopt; };
+    const bool silu = ctx->saved_data["silu"].toBool(), ret_final = ctx->saved_data["final"].toBool();
+    c10::optional<at::Tensor> dfinal;
+    if (ret_final && grads.size() > 1 && grads[1].defined()) dfinal = grads[1].contiguous();
+    const bool need_dinit =
+        init.defined() && ctx->needs_input_grad(static_cast<size_t>(ctx->saved_data["init_edge"].toInt()));
+    at::Tensor dout = grads[0];
+    if (!dout.defined()) dout = at::zeros_like(x);
+    dout = tma_layout(dout, weight.size(1));
+    auto [rc, dx, dweight, dbias, dinit] =
+        bwd(x, weight, opt(bias), opt(seq_idx), opt(init), dout, dfinal, need_dinit, silu, c10::nullopt, true);
+    check_rc(rc, "causal_conv1d backward");
+    return {dx, dweight.value_or(at::Tensor()), dbias.value_or(at::Tensor()), at::Tensor(),
+            dinit.value_or(at::Tensor()), at::Tensor(), at::Tensor()};
+  }
+};
+
+torch::autograd::variable_list conv_fn(const at::Tensor& x, const at::Tensor& weight,
+                                       const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& seq_idx,
+                                       const c10::optional<at::Tensor>& initial_states, bool return_final_states,
+                                       bool silu) {
+  return ConvFn::apply(x, weight, bias, seq_idx, initial_states, return_final_states, silu);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "torch-side launchers of libcausal_conv1d_b200 (forward and backward)";
   m.def("fwd", &fwd, "(rc, out) = fwd(x, weight, bias, seq_idx, initial_states, final_states, silu)");
+  m.def("conv_fn", &conv_fn,
+        "[out] or [out, final_states] = conv_fn(x, weight, bias, seq_idx, initial_states, return_final_states, "
+        "silu): forward with autograd");
   m.def("bwd", &bwd,
         "(rc, dx, dweight, dbias, dinit) = bwd(x, weight, bias, seq_idx, initial_states, dout, dfinal_states, "
         "need_dinit, silu, grad_f32, fuse_param_grads)");
