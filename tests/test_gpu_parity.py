@@ -289,6 +289,31 @@ def test_deterministic_weight_grads(cc):
         assert torch.equal(a, c)
 
 
+@pytest.mark.parametrize("bias", [True, False])
+def test_fp32_gradient_vector_output(cc, bias):
+    """The backward's fp32 [dweight (D, W), dbias (D)] output (`grad_f32`, what the data-parallel
+    path all-reduces) holds the same bits as the ordinary dweight/dbias outputs; dx is unchanged
+    and dweight/dbias are not returned."""
+    gen = torch.Generator().manual_seed(5)
+    D, W = 512, 8
+    x = torch.randn(2, 3000, D, generator=gen).to(torch.bfloat16).to(DEV)
+    w = torch.randn(D, W, generator=gen).to(DEV)
+    b = torch.randn(D, generator=gen).to(DEV) if bias else None
+    dy = torch.randn(2, 3000, D, generator=gen).to(torch.bfloat16).to(DEV)
+    from causal_conv1d_b200.causal_conv1d import _bwd
+
+    dx, dw, db, _ = _bwd(x, w, b, None, None, dy, None, False, True)
+    flat = torch.full((D * (W + 1),), float("nan"), device=DEV)
+    dx2, dw2, db2, _ = _bwd(x, w, b, None, None, dy, None, False, True, grad_f32=flat)
+    assert dw2 is None and db2 is None
+    assert torch.equal(dx2, dx)
+    assert torch.equal(flat[: D * W].view(D, W), dw)
+    if bias:
+        assert torch.equal(flat[D * W:], db)
+    else:
+        assert bool((flat[D * W:] == 0).all()), "dbias part of the vector is zero without bias"
+
+
 def test_status_word_clear(cc):
     from causal_conv1d_b200 import _native
 
